@@ -1,0 +1,426 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 selective scan on BASELINE.json's headline workload.
+
+Default workload (N=1 and per rank for N>1): config 3, the Mamba-2.8B-like training step
+of the selective scan, fp16 I/O, B=4, L=2048, D=5120, N=16, forward + backward through
+the public API (SelectiveScanCuda -> SelectiveScanFnV2). Metric: GB/s of algorithmic bytes
+(fwd reads u, delta, B, C, A, D and writes y; bwd reads u, delta, dy, B, C, A, D and writes
+du, ddelta, dA, dB, dC, dD), with the roofline fraction against the slower of HBM
+(bytes / measured HBM bandwidth) and MUFU (16 ex2 per (b, l, d) element per pass).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                  [--config c3|c2|c1|c4|c5]
+
+For N > 1 launch with torchrun (one process per GPU, NCCL): every rank scans its own
+batch (weak scaling, no data-path collective); time = max over ranks of the device time.
+``--impl reference`` times the reference algorithm's CPU restatement (oracle/, float64,
+all host threads) on a bounded sample of the same workload (rank 0 only).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG_PARENT = os.path.join(ROOT, "mamba-windows-cuda_b200")
+for _p in (ROOT, PKG_PARENT):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+METRIC = "selective-scan fwd+bwd GB/s & % of HBM/MUFU roofline, B=4 L=2048 D=5120 fp16"
+NSTATE = 16
+
+CONFIGS = {
+    "c3": dict(workload="config 3: Mamba-2.8B-like training step, selective scan fwd+bwd "
+                        "(SelectiveScanCuda, default V2 path)",
+               B=4, L=2048, D=5120, dtype=torch.float16, mode="fwdbwd", dist="c3"),
+    "c1": dict(workload="config 1: selective scan fwd+bwd fp32 B1 L1024 D256",
+               B=1, L=1024, D=256, dtype=torch.float32, mode="fwdbwd", dist="c1"),
+    "c2": dict(workload="config 2: Mamba-1.4B-like inference forward_with_state fp16",
+               B=8, L=2048, D=4096, dtype=torch.float16, mode="fwd", dist="c2"),
+    "c4": dict(workload="config 4: streaming scan fp32, 16 chunks of 65536 with h_prev/h_last",
+               B=1, L=65536, D=2048, dtype=torch.float32, mode="stream", dist="c4", chunks=16),
+    "c5": dict(workload="config 5: parallel_scan_fn fp32 (16, 1024, 16384, 1)",
+               B=16, L=16384, D=1024, dtype=torch.float32, mode="pscan", dist="c5"),
+}
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            pk = json.load(f)
+        return dict(hbm_gbs=float(pk["hbm_gbs"]), sm_max_mhz=float(pk.get("sm_max_mhz", 1965.0)),
+                    source="measured (MEASURED_PEAKS.json)")
+    except Exception:
+        return dict(hbm_gbs=6650.0, sm_max_mhz=1965.0, source="fallback")
+
+
+# ----------------------------------------------------------------------------- models
+
+def ss_bytes(B, L, D, es, mode):
+    """Algorithmic bytes of one forward (+ backward) pass."""
+    E = B * L * D
+    bc = B * L * NSTATE * es
+    params = (D * NSTATE + D) * es
+    fwd = 3 * E * es + 2 * bc + params
+    if mode in ("fwd", "stream"):
+        return fwd + (2 * B * D * NSTATE * es)  # h_prev in / h_last out
+    bwd = 5 * E * es + 4 * bc + 2 * params
+    return fwd + bwd
+
+
+def ss_ex2(B, L, D, mode):
+    E = B * L * D
+    return 16 * E * (2 if mode == "fwdbwd" else 1)
+
+
+# ----------------------------------------------------------------------------- inputs
+
+def make_ss_inputs(cfg, dev, seed, L=None, D=None, B=None):
+    B = cfg["B"] if B is None else B
+    L = cfg["L"] if L is None else L
+    D = cfg["D"] if D is None else D
+    g = torch.Generator(device=dev).manual_seed(seed)
+    f32 = torch.float32
+    n1 = torch.arange(1, NSTATE + 1, dtype=f32, device=dev)
+
+    def rn(*s):
+        return torch.randn(*s, generator=g, device=dev, dtype=f32)
+
+    dist = cfg["dist"]
+    if dist in ("c1", "c3"):
+        u, delta = rn(B, L, D), torch.nn.functional.softplus(rn(B, L, D) * 0.5 - 1.0)
+        A, Bm, Cm, Dv = -n1.repeat(D, 1), rn(B, L, NSTATE), rn(B, L, NSTATE), torch.ones(D, device=dev)
+    elif dist == "c2":
+        u, delta = rn(B, L, D), torch.nn.functional.softplus(rn(B, L, D) * 0.5 - 2.0)
+        A = -n1.repeat(D, 1) * (1 + 0.1 * torch.rand(D, NSTATE, generator=g, device=dev))
+        Bm, Cm = rn(B, L, NSTATE) / 4, rn(B, L, NSTATE) / 4
+        Dv = 0.5 + torch.rand(D, generator=g, device=dev)
+    else:  # c4
+        u, delta = rn(B, L, D), torch.nn.functional.softplus(rn(B, L, D) * 0.5 - 3.0)
+        A, Bm, Cm, Dv = -(n1 / 16).repeat(D, 1), rn(B, L, NSTATE), rn(B, L, NSTATE), torch.ones(D, device=dev)
+    dt = cfg["dtype"]
+    return [t.to(dt).contiguous() for t in (u, delta, A, Bm, Cm, Dv)], rn(B, L, D).to(dt)
+
+
+# ----------------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+               0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x100: "display_clock_setting"}
+
+    def __init__(self, index):
+        self.index = index
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.ok = False
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self._t is not None:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
+        names = [n for bit, n in self.REASONS.items() if self.reasons & bit and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": names, "samples": len(self.samples)}
+
+
+# ----------------------------------------------------------------------------- timing
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        backend = "nccl" if args.impl == "b200" else "gloo"
+        if args.impl == "b200":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+    return world, rank, local
+
+
+def barrier_sync(world, dev):
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.zeros(1, device=dev)
+        dist.all_reduce(t)
+    torch.cuda.synchronize(dev)
+
+
+def max_over_ranks(x, world, dev):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x, world, dev):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------- CPU side
+
+def oracle_sample(cfg, target_s, seed=0):
+    """Time the float64 CPU restatement of the reference path on an L-slice of the
+    workload sized to ~target_s seconds. Returns (seconds, bytes, sample_desc, threads)."""
+    from oracle import oracle as O
+    import numpy as np
+    B, D = cfg["B"], cfg["D"]
+    es = torch.tensor([], dtype=cfg["dtype"]).element_size()
+
+    def run(Ls):
+        (u, delta, A, Bm, Cm, Dv), gy = make_ss_inputs(cfg, "cpu", seed, L=Ls)
+        n = [t.double().numpy() for t in (u, delta, A, Bm, Cm, Dv)]
+        t0 = time.perf_counter()
+        O.ss_fwd(*n)
+        if cfg["mode"] == "fwdbwd":
+            O.ss_bwd(*n, gy.double().numpy())
+        return time.perf_counter() - t0
+
+    probe = 16
+    t = run(probe)
+    Ls = int(min(cfg["L"], max(16, probe * target_s / max(t, 1e-6))))
+    secs = run(Ls)
+    nbytes = ss_bytes(B, Ls, D, es, cfg["mode"])
+    desc = (f"B={B} L={Ls} (of {cfg['L']}) D={D} slice, float64 oracle on "
+            f"{'fp16-valued' if es == 2 else 'fp32'} inputs, fwd{'+bwd' if cfg['mode'] == 'fwdbwd' else ''}")
+    return secs, nbytes, desc, O.num_threads()
+
+
+def reference_arm(args, cfg):
+    """Times the reference algorithm (CPU restatement in oracle/) on host cores."""
+    from oracle import oracle as O
+    O.build()
+    per_step = max(0.2, 90.0 / max(1, args.steps + args.warmup))
+    secs, nbytes, desc, threads = oracle_sample(cfg, per_step)
+    times = []
+    for i in range(args.warmup + args.steps):
+        s2, b2, _, _ = oracle_sample(cfg, per_step, seed=i)
+        if i >= args.warmup:
+            times.append((s2, b2))
+    tot_s = sum(t for t, _ in times)
+    tot_b = sum(b for _, b in times)
+    gbs = tot_b / tot_s / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * tot_s / len(times),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic (seeded, BASELINE distributions)",
+        "config": {"workload": cfg["workload"], "B": cfg["B"], "L": cfg["L"], "D": cfg["D"],
+                   "N": NSTATE, "sample_per_step": desc},
+        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- GPU arms
+
+def bench_fwdbwd(args, cfg, dev, world, rank, peaks):
+    import mamba_windows_cuda as mwc
+    B, L, D = cfg["B"], cfg["L"], cfg["D"]
+    ins, gy = make_ss_inputs(cfg, dev, seed=1000 + rank)
+    es = ins[0].element_size()
+    leaves = [t.clone().requires_grad_(True) for t in ins]
+    mod = mwc.SelectiveScanCuda()
+    stream = torch.cuda.current_stream(dev)
+
+    def step(ev=None):
+        for t in leaves:
+            t.grad = None
+        if ev is not None:
+            ev[0].record(stream)
+        out = mod(*leaves)
+        if ev is not None:
+            ev[1].record(stream)
+        out.backward(gy)
+        if ev is not None:
+            ev[2].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier_sync(world, dev)
+    with ClockSampler(dev.index if dev.index is not None else 0) as clk:
+        start.record(stream)
+        for i in range(args.steps):
+            step(evs[i])
+        stop.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier_sync(world, dev)
+    ms = start.elapsed_time(stop)
+    fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    ms_max = max_over_ranks(ms, world, dev)
+    nbytes = ss_bytes(B, L, D, es, "fwdbwd")
+    value = nbytes * world / (ms_max / args.steps / 1e3) / 1e9
+    launches_per_step = 3 if int(mwc._lib.load().mwc_ss_fwd_workspace_bytes(B, L, D, 1 if es == 2 else 0)) == 0 else 4
+
+    # roofline of the dominant kernel (the backward: reverse scan + its fixed-order reduction)
+    mufu_peak = 148 * 16 * peaks["sm_max_mhz"] * 1e6  # ex2 / s at the max SM clock
+    E = B * L * D
+    bwd_bytes = ss_bytes(B, L, D, es, "fwdbwd") - ss_bytes(B, L, D, es, "fwd") + 2 * B * D * NSTATE * es
+    fwd_bytes = nbytes - bwd_bytes
+
+    def roof(nb, nex2, t_ms):
+        t = t_ms / 1e3
+        return dict(hbm_gbs=nb / t / 1e9, hbm_frac=nb / t / 1e9 / peaks["hbm_gbs"],
+                    ex2_per_s=nex2 / t, mufu_frac=nex2 / t / mufu_peak,
+                    frac=max(nb / (peaks["hbm_gbs"] * 1e9), nex2 / mufu_peak) / t)
+
+    rb = roof(bwd_bytes, 16 * E, bwd_ms)
+    rf = roof(fwd_bytes, 16 * E, fwd_ms)
+    rs = roof(nbytes, 32 * E, ms / args.steps)
+    roofline = {
+        "kernel": "ss_bwd_kernel + ss_bwd_final_kernel (backward op)",
+        "bound": "mufu", "achieved": rb["ex2_per_s"] / 1e9, "peak": mufu_peak / 1e9,
+        "unit": "Gex2/s", "frac": rb["mufu_frac"], "traffic": None,
+        "hbm": {"achieved": rb["hbm_gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": rb["hbm_frac"], "peak_source": peaks["source"]},
+        "model": "max(algorithmic bytes / HBM, 16 ex2 per element / MUFU at 148 SM x 16/clk x sm_max_mhz)",
+        "per_op_ms": {"fwd": fwd_ms, "bwd": bwd_ms},
+        "fwd_frac": rf["frac"], "step_frac": rs["frac"],
+    }
+
+    # e2e through the public API from pinned host memory
+    host_in = [t.detach().cpu().pin_memory() for t in ins]
+    host_g = gy.cpu().pin_memory()
+    host_out = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in ins]
+    h2d = sum(t.numel() * t.element_size() for t in host_in) + host_g.numel() * host_g.element_size()
+    d2h = sum(t.numel() * t.element_size() for t in host_out)
+
+    def e2e_step():
+        xs = [h.to(dev, non_blocking=True).requires_grad_(True) for h in host_in]
+        g_d = host_g.to(dev, non_blocking=True)
+        out = mod(*xs)
+        out.backward(g_d)
+        for ho, x in zip(host_out, xs):
+            ho.copy_(x.grad, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 10))
+    for _ in range(2):
+        e2e_step()
+    barrier_sync(world, dev)
+    s2, t2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    t2.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(s2.elapsed_time(t2), world, dev) / e2e_steps
+    e2e = {"value": nbytes * world / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
+           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms}
+    return dict(value=value, ms_per_step=ms_max / args.steps, roofline=roofline, e2e=e2e,
+                clocks=clk.summary(), gpu_launches=launches_per_step * args.steps,
+                dtype="f32", io_dtype=str(cfg["dtype"]).replace("torch.", ""))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c3")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    cfg = CONFIGS[args.config]
+    world, rank, local = dist_setup(args)
+    peaks = load_peaks()
+
+    if args.impl == "reference":
+        if rank == 0:
+            reference_arm(args, cfg)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if cfg["mode"] != "fwdbwd":
+        raise SystemExit(f"--config {args.config}: use the per-config scripts in the tests; "
+                         "bench.py measures the fwd+bwd workloads")
+    res = bench_fwdbwd(args, cfg, dev, world, rank, peaks)
+
+    line = {
+        "metric": METRIC, "value": res["value"], "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": res["dtype"], "data": "synthetic (seeded, BASELINE distributions, generated on device)",
+        "config": {"workload": cfg["workload"], "B": cfg["B"], "L": cfg["L"], "D": cfg["D"],
+                   "N": NSTATE, "io_dtype": res["io_dtype"],
+                   "l2": "inputs + outputs per step (~250 MB at config 3) exceed the 126 MB L2; no flush",
+                   "parallelism": f"replicas x{world}: one independent batch per rank, no collective"},
+        "roofline": res["roofline"], "e2e": res["e2e"], "gpu_launches": res["gpu_launches"],
+        "clocks": res["clocks"],
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        secs, nbytes, desc, threads = oracle_sample(cfg, 10.0)
+        line["cpu_baseline"] = {"value": nbytes / secs / 1e9, "unit": "GB/s", "cores": threads,
+                                "kind": "port", "sample": desc}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

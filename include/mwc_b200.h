@@ -1,0 +1,133 @@
+/*
+ * mwc_b200.h -- C ABI of the B200 (sm_100a) selective-scan library libmwc_b200.so.
+ *
+ * Drop-in native boundary for the hot path of zouyuanqing/mamba-windows-cuda
+ * (N = 16 selective scan, forward + backward with h_prev / h_last streaming, and the
+ * first-order linear-recurrence scan behind parallel_scan_fn). Every entry point takes
+ * plain device pointers, int64 sizes, a dtype code and a cudaStream_t passed as void*.
+ * Nothing is allocated inside the library: outputs and workspaces come from the caller
+ * (the Python layer allocates them with the PyTorch caching allocator). Calls are
+ * reentrant; the only global state is the per-thread error message.
+ *
+ * All tensors are contiguous row-major with these shapes (N = 16 states):
+ *   u, delta, out, du, ddelta, dout : (B, L, D)
+ *   A, dA : (D, 16)      Bm, Cm, dB, dC : (B, L, 16)      Dv, dD : (D)
+ *   h_prev, h_last, dh_last, dh_prev : (B, D, 16)          (same dtype as u)
+ *   ckpt  : (B, nck, D, 16) float32, nck = mwc_ss_ckpt_count(L); ckpt[b, k] is the state
+ *           after step min(16 (k + 1), L) - 1
+ *   decay, h_in : (B, D, 16) float32
+ * All floating tensors of one call share one dtype (MWC_F32 or MWC_F16) except the
+ * float32 ckpt / decay / h_in buffers; arithmetic is float32 throughout.
+ *
+ * Return value: MWC_OK (0) or an MWC_ERR_* code; mwc_last_error() then gives the message
+ * (same wording as the reference's TORCH_CHECKs where one exists).
+ */
+#ifndef MWC_B200_H
+#define MWC_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MWC_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define MWC_API __attribute__((visibility("default")))
+#else
+#define MWC_API
+#endif
+
+enum mwc_dtype { MWC_F32 = 0, MWC_F16 = 1 };
+
+enum mwc_status {
+    MWC_OK = 0,
+    MWC_ERR_INVALID = 1,    /* bad pointer, shape or dtype (reference: TORCH_CHECK -> RuntimeError) */
+    MWC_ERR_UNSUPPORTED = 2,/* valid request this build does not implement */
+    MWC_ERR_WORKSPACE = 3,  /* workspace missing or smaller than the *_workspace_bytes query */
+    MWC_ERR_CUDA = 4,       /* a CUDA launch or runtime call failed */
+    MWC_ERR_TIMEOUT = 5     /* a bounded device-side wait gave up (no GPU fault is raised) */
+};
+
+/* Library identity and error reporting. */
+MWC_API int mwc_abi_version(void);
+MWC_API const char* mwc_last_error(void);            /* message of the last failed call on this thread */
+MWC_API const char* mwc_build_info(void);            /* compiler / arch string of this build */
+
+/* Number of float32 checkpoint states per channel for a sequence of length L (ceil(L/16)). */
+MWC_API int64_t mwc_ss_ckpt_count(int64_t L);
+
+/* Workspace bytes mwc_ss_fwd needs for (B, L, D) on the current device (0 when the
+ * whole sequence is scanned by one pass; > 0 when it is split along L). */
+MWC_API int64_t mwc_ss_fwd_workspace_bytes(int64_t B, int64_t L, int64_t D, int dtype);
+
+/*
+ * Forward selective scan: h_t = exp(delta_t * A) h_{t-1} + delta_t u_t B_t,
+ * out_t = <C_t, h_t> + Dv * u_t, h_{-1} = h_prev (or 0 when NULL).
+ * Replaces selective_scan_cuda_forward / _forward_with_state / _forward_store
+ * (mamba_windows_cuda/mamba_cuda.py:176-269, 271-359, 747-764) and
+ * fused_selective_scan_forward (mamba_windows_cuda/selective_scan_cuda_ext.py:389-452).
+ * Optional outputs (NULL to skip): out, h_last (dtype), ckpt (float32 states every 16 steps,
+ * what the backward reads), decay = exp(A * sum_t delta_t) (float32, the segment decay an
+ * L-sharded caller combines). out may be NULL to only produce checkpoints (recompute for
+ * checkpoint level 1). The exponent is clamped to [-88, 88] like safe_exp
+ * (mamba_cuda.py:65-70).
+ */
+MWC_API int mwc_ss_fwd(const void* u, const void* delta, const void* A, const void* Bm, const void* Cm,
+               const void* Dv, const void* h_prev, void* out, void* h_last, float* ckpt,
+               float* decay, void* workspace, int64_t workspace_bytes,
+               int64_t B, int64_t L, int64_t D, int dtype, void* stream);
+
+/* Workspace bytes mwc_ss_bwd needs for (B, L, D) on the current device. */
+MWC_API int64_t mwc_ss_bwd_workspace_bytes(int64_t B, int64_t L, int64_t D, int dtype);
+
+/*
+ * Backward of mwc_ss_fwd for loss = sum(out * dout) + sum(h_last * dh_last): a reverse scan
+ * that recomputes states chunk by chunk from ckpt (required when L > 16) and h_prev.
+ * Produces du, ddelta (B, L, D), dA (D, 16), dB, dC (B, L, 16), dD (D) in dtype and, when
+ * dh_prev != NULL, dh_prev (B, D, 16). dh_last may be NULL (zero). All reductions run in a
+ * fixed order, so results are bitwise reproducible.
+ * Replaces selective_scan_cuda_backward / _backward_direct (mamba_cuda.py:564-604, 766-790),
+ * the stateful PyTorch backward selective_scan_backward (mamba_cuda.py:949-1041) and the
+ * extension's selective_scan_backward (selective_scan_cuda_ext.py:454-514).
+ */
+MWC_API int mwc_ss_bwd(const void* u, const void* delta, const void* A, const void* Bm, const void* Cm,
+               const void* Dv, const void* h_prev, const void* dout, const void* dh_last,
+               const float* ckpt, void* du, void* ddelta, void* dA, void* dB, void* dC, void* dD,
+               void* dh_prev, void* workspace, int64_t workspace_bytes,
+               int64_t B, int64_t L, int64_t D, int dtype, void* stream);
+
+/*
+ * Fold a known incoming state into a scan that was run from zero (sequence sharding along
+ * L): with Pcum_t = exp(A * sum_{s<=t} delta_s),
+ *   out_t  += <C_t, Pcum_t * h_in>            (out may be NULL)
+ *   ckpt_k += Pcum_{t_k} * h_in               (ckpt may be NULL)
+ *   h_last  = decay * h_in + h_last           (h_last may be NULL; decay required then)
+ * The out/ckpt loop stops once every state has decayed below 2^-40 of h_in (never when an
+ * exponent A*delta is positive or a delta is negative). No reference counterpart: the
+ * reference has no sequence sharding; this is the carry fixup of the L-sharded scan.
+ */
+MWC_API int mwc_ss_fixup(const void* delta, const void* A, const void* Cm, const float* h_in,
+                 const float* decay, void* out, void* h_last, float* ckpt,
+                 int64_t B, int64_t L, int64_t D, int dtype, void* stream);
+
+/*
+ * First-order linear recurrence along axis 2 of (B, D, L, N) = (R, L, N) with R = B*D:
+ * h_0 = x_0 (a_0 ignored), h_t = a_t h_{t-1} + x_t. Replaces PScan.forward /
+ * parallel_scan_fn (mamba_windows_cuda/pscan.py:16-150), with the semantics of
+ * parallel_scan_ref (pscan.py:153-171).
+ */
+MWC_API int mwc_lin_scan_fwd(const void* a, const void* x, void* h, int64_t R, int64_t L, int64_t N,
+                     int dtype, void* stream);
+
+/* Gradient of mwc_lin_scan_fwd for loss = sum(h * g): gx_t = g_t + a_{t+1} gx_{t+1},
+ * ga_t = gx_t h_{t-1}, ga_0 = 0. Replaces PScan.backward (pscan.py:98-136). */
+MWC_API int mwc_lin_scan_bwd(const void* a, const void* h, const void* g, void* ga, void* gx,
+                     int64_t R, int64_t L, int64_t N, int dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MWC_B200_H */

@@ -1,0 +1,270 @@
+// extern "C" entry points of libmwc_b200.so (declared in include/mwc_b200.h).
+//
+// Each entry point validates its arguments (messages follow the reference's TORCH_CHECK
+// wording, mamba_windows_cuda/mamba_cuda.py:186-238), carves the caller's workspace,
+// picks a launch plan for the current device and enqueues the kernels on the given stream.
+// Nothing is allocated here and nothing blocks the host.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+
+#include "mwc_b200.h"
+#include "mwc_device.cuh"
+#include "mwc_internal.h"
+
+using namespace mwc;
+
+#define MWC_XSTR(x) #x
+#define MWC_STR(x) MWC_XSTR(x)
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int ok() {
+    g_err[0] = '\0';
+    return MWC_OK;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+    return fail(MWC_ERR_CUDA, "%s: %s (%s)", where, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+int device_sms() {
+    static int cache[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    if (dev >= 0 && dev < 64 && cache[dev] > 0) return cache[dev];
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+        n = 148;
+    if (dev >= 0 && dev < 64) cache[dev] = n;
+    return n;
+}
+
+size_t elem_size(int dtype) { return dtype == MWC_F16 ? 2 : 4; }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
+
+// Workspace layout of the backward: [ws_bc | ws_a | ws_d], each 256-byte aligned.
+struct BwdWs {
+    int64_t nblk, off_a, off_d, total;
+};
+
+BwdWs bwd_ws(int64_t B, int64_t L, int64_t D, int dtype) {
+    BwdWs w;
+    const int64_t cpb = bwd_channels_per_block(dtype);
+    const int64_t nck = (L + CK - 1) / CK;
+    w.nblk = (D + cpb - 1) / cpb;
+    const int64_t bc = w.nblk * B * nck * CK * 2 * NSTATE * 4;
+    w.off_a = align_up(bc, 256);
+    w.off_d = align_up(w.off_a + B * D * NSTATE * 4, 256);
+    w.total = align_up(w.off_d + B * D * 4, 256);
+    return w;
+}
+
+int check_dtype(int dtype) {
+    if (dtype != MWC_F32 && dtype != MWC_F16)
+        return fail(MWC_ERR_INVALID, "u must be float32/float16 (dtype code %d)", dtype);
+    return MWC_OK;
+}
+
+int check_sizes(int64_t B, int64_t L, int64_t D) {
+    if (B < 0 || L < 0 || D < 0)
+        return fail(MWC_ERR_INVALID, "negative size (B=%lld, L=%lld, D=%lld)", (long long)B,
+                    (long long)L, (long long)D);
+    if (L == 0) return fail(MWC_ERR_INVALID, "empty sequence (L=0)");
+    if (B > 65535) return fail(MWC_ERR_UNSUPPORTED, "batch %lld exceeds 65535", (long long)B);
+    if ((D + 3) / 4 > 0x7fffffffLL) return fail(MWC_ERR_UNSUPPORTED, "D too large");
+    return MWC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mwc_abi_version(void) { return MWC_ABI_VERSION; }
+
+const char* mwc_last_error(void) { return g_err; }
+
+const char* mwc_build_info(void) {
+    return "libmwc_b200: sm_100a, CUDA " MWC_STR(__CUDACC_VER_MAJOR__) "." MWC_STR(
+        __CUDACC_VER_MINOR__);
+}
+
+int64_t mwc_ss_ckpt_count(int64_t L) { return L <= 0 ? 0 : (L + CK - 1) / CK; }
+
+int64_t mwc_ss_fwd_workspace_bytes(int64_t B, int64_t L, int64_t D, int dtype) {
+    if (B <= 0 || L <= 0 || D <= 0) return 0;
+    const FwdPlan plan = plan_fwd(B, L, D, dtype, device_sms());
+    return align_up(fwd_carry_floats(plan, B, D) * 4, 256);
+}
+
+int mwc_ss_fwd(const void* u, const void* delta, const void* A, const void* Bm, const void* Cm,
+               const void* Dv, const void* h_prev, void* out, void* h_last, float* ckpt,
+               float* decay, void* workspace, int64_t workspace_bytes, int64_t B, int64_t L,
+               int64_t D, int dtype, void* stream) {
+    int rc;
+    if ((rc = check_dtype(dtype)) != MWC_OK) return rc;
+    if ((rc = check_sizes(B, L, D)) != MWC_OK) return rc;
+    if (!u || !delta || !A || !Bm || !Cm || !Dv)
+        return fail(MWC_ERR_INVALID, "u, delta, A, B_ssm, C_ssm and D_ssm are required");
+    if (!out && !h_last && !ckpt && !decay)
+        return fail(MWC_ERR_INVALID, "no output requested");
+    if (B == 0 || D == 0) return ok();
+    const FwdPlan plan = plan_fwd(B, L, D, dtype, device_sms());
+    const int64_t need = align_up(fwd_carry_floats(plan, B, D) * 4, 256);
+    if (need > 0 && (!workspace || workspace_bytes < need))
+        return fail(MWC_ERR_WORKSPACE, "forward workspace of %lld bytes required, got %lld",
+                    (long long)need, (long long)workspace_bytes);
+    const size_t es = elem_size(dtype);
+    FwdArgs a{};
+    a.u = u; a.delta = delta; a.A = A; a.Bm = Bm; a.Cm = Cm; a.Dv = Dv;
+    a.h_prev = h_prev; a.out = out; a.h_last = h_last; a.ckpt = ckpt; a.decay = decay;
+    a.carry = plan.nseg > 1 ? static_cast<float*>(workspace) : nullptr;
+    a.B = B; a.L = L; a.D = D;
+    a.seg_len = plan.seg_len; a.nseg = plan.nseg;
+    a.nck = (int)mwc_ss_ckpt_count(L);
+    a.vec = ((D * (int64_t)es) % 16 == 0) && aligned16(u) && aligned16(delta) &&
+            (!out || aligned16(out));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = launch_fwd(a, plan, dtype, s);
+    if (e != cudaSuccess) return cuda_fail(e, "selective-scan forward launch");
+    if (plan.nseg > 1) {
+        FixupArgs f{};
+        f.delta = delta; f.A = A; f.Cm = Cm; f.carry = a.carry;
+        f.out = out; f.h_last = h_last; f.decay_out = decay; f.ckpt = ckpt;
+        f.B = B; f.L = L; f.D = D; f.seg_len = plan.seg_len; f.nseg = plan.nseg;
+        f.nck = a.nck; f.mode = 0; f.vec = a.vec;
+        e = launch_fixup(f, plan, dtype, s);
+        if (e != cudaSuccess) return cuda_fail(e, "selective-scan segment fixup launch");
+    }
+    return ok();
+}
+
+int64_t mwc_ss_bwd_workspace_bytes(int64_t B, int64_t L, int64_t D, int dtype) {
+    if (B <= 0 || L <= 0 || D <= 0) return 0;
+    return bwd_ws(B, L, D, dtype).total;
+}
+
+int mwc_ss_bwd(const void* u, const void* delta, const void* A, const void* Bm, const void* Cm,
+               const void* Dv, const void* h_prev, const void* dout, const void* dh_last,
+               const float* ckpt, void* du, void* ddelta, void* dA, void* dB, void* dC, void* dD,
+               void* dh_prev, void* workspace, int64_t workspace_bytes, int64_t B, int64_t L,
+               int64_t D, int dtype, void* stream) {
+    int rc;
+    if ((rc = check_dtype(dtype)) != MWC_OK) return rc;
+    if ((rc = check_sizes(B, L, D)) != MWC_OK) return rc;
+    if (!u || !delta || !A || !Bm || !Cm || !Dv || !dout)
+        return fail(MWC_ERR_INVALID, "u, delta, A, B_ssm, C_ssm, D_ssm and dout are required");
+    if (!du || !ddelta || !dA || !dB || !dC || !dD)
+        return fail(MWC_ERR_INVALID, "du, ddelta, dA, dB, dC and dD outputs are required");
+    const int64_t nck = mwc_ss_ckpt_count(L);
+    if (nck > 1 && !ckpt)
+        return fail(MWC_ERR_INVALID, "checkpoint states are required when L > %d", CK);
+    if (B == 0 || D == 0) return ok();
+    const BwdWs w = bwd_ws(B, L, D, dtype);
+    if (!workspace || workspace_bytes < w.total)
+        return fail(MWC_ERR_WORKSPACE, "backward workspace of %lld bytes required, got %lld",
+                    (long long)w.total, (long long)workspace_bytes);
+    if (!aligned16(workspace))
+        return fail(MWC_ERR_WORKSPACE, "backward workspace must be 16-byte aligned");
+    const size_t es = elem_size(dtype);
+    char* ws = static_cast<char*>(workspace);
+    BwdArgs a{};
+    a.u = u; a.delta = delta; a.A = A; a.Bm = Bm; a.Cm = Cm; a.Dv = Dv;
+    a.h_prev = h_prev; a.dout = dout; a.dh_last = dh_last; a.ckpt = ckpt;
+    a.du = du; a.ddelta = ddelta; a.dh_prev = dh_prev;
+    a.ws_bc = reinterpret_cast<float*>(ws);
+    a.ws_a = reinterpret_cast<float*>(ws + w.off_a);
+    a.ws_d = reinterpret_cast<float*>(ws + w.off_d);
+    a.B = B; a.L = L; a.D = D; a.nck = (int)nck; a.nblk = (int)w.nblk;
+    a.vec = ((D * (int64_t)es) % 16 == 0) && aligned16(u) && aligned16(delta) &&
+            aligned16(dout) && aligned16(du) && aligned16(ddelta);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = launch_bwd(a, dtype, s);
+    if (e != cudaSuccess) return cuda_fail(e, "selective-scan backward launch");
+    BwdFinalArgs f{};
+    f.ws_bc = a.ws_bc; f.ws_a = a.ws_a; f.ws_d = a.ws_d;
+    f.dA = dA; f.dB = dB; f.dC = dC; f.dD = dD;
+    f.B = B; f.L = L; f.D = D; f.nck = (int)nck; f.nblk = (int)w.nblk;
+    e = launch_bwd_final(f, dtype, s);
+    if (e != cudaSuccess) return cuda_fail(e, "selective-scan backward reduction launch");
+    return ok();
+}
+
+int mwc_ss_fixup(const void* delta, const void* A, const void* Cm, const float* h_in,
+                 const float* decay, void* out, void* h_last, float* ckpt, int64_t B, int64_t L,
+                 int64_t D, int dtype, void* stream) {
+    int rc;
+    if ((rc = check_dtype(dtype)) != MWC_OK) return rc;
+    if ((rc = check_sizes(B, L, D)) != MWC_OK) return rc;
+    if (!delta || !A || !h_in) return fail(MWC_ERR_INVALID, "delta, A and h_in are required");
+    if (out && !Cm) return fail(MWC_ERR_INVALID, "C_ssm is required to correct the output");
+    if (h_last && !decay) return fail(MWC_ERR_INVALID, "decay is required to correct h_last");
+    if (B == 0 || D == 0) return ok();
+    FwdPlan plan = plan_fwd(B, L, D, dtype, device_sms());
+    plan.nseg = 1;
+    plan.seg_len = L;
+    const size_t es = elem_size(dtype);
+    FixupArgs f{};
+    f.delta = delta; f.A = A; f.Cm = Cm; f.h_in = h_in; f.decay = decay;
+    f.out = out; f.h_last = h_last; f.ckpt = ckpt;
+    f.B = B; f.L = L; f.D = D; f.seg_len = L; f.nseg = 1;
+    f.nck = (int)mwc_ss_ckpt_count(L); f.mode = 1;
+    f.vec = ((D * (int64_t)es) % 16 == 0) && aligned16(delta) && (!out || aligned16(out));
+    cudaError_t e = launch_fixup(f, plan, dtype, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "selective-scan fixup launch");
+    return ok();
+}
+
+int mwc_lin_scan_fwd(const void* a, const void* x, void* h, int64_t R, int64_t L, int64_t N,
+                     int dtype, void* stream) {
+    int rc;
+    if ((rc = check_dtype(dtype)) != MWC_OK) return rc;
+    if (R < 0 || L < 0 || N < 0) return fail(MWC_ERR_INVALID, "negative size");
+    if (!a || !x || !h) return fail(MWC_ERR_INVALID, "A, X and the output are required");
+    if (R == 0 || L == 0 || N == 0) return ok();
+    if ((R + 3) / 4 > 0x7fffffffLL || (N + 31) / 32 > 65535)
+        return fail(MWC_ERR_UNSUPPORTED, "scan shape too large");
+    const size_t es = elem_size(dtype);
+    LinArgs la{};
+    la.a = a; la.x = x; la.out_h = h; la.R = R; la.L = L; la.N = N;
+    la.vec = (N == 1) && ((L * (int64_t)es) % 16 == 0) && aligned16(a) && aligned16(x) &&
+             aligned16(h);
+    cudaError_t e = launch_lin_fwd(la, dtype, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "linear scan forward launch");
+    return ok();
+}
+
+int mwc_lin_scan_bwd(const void* a, const void* h, const void* g, void* ga, void* gx, int64_t R,
+                     int64_t L, int64_t N, int dtype, void* stream) {
+    int rc;
+    if ((rc = check_dtype(dtype)) != MWC_OK) return rc;
+    if (R < 0 || L < 0 || N < 0) return fail(MWC_ERR_INVALID, "negative size");
+    if (!a || !h || !g || !ga || !gx)
+        return fail(MWC_ERR_INVALID, "A, H, grad and both gradient outputs are required");
+    if (R == 0 || L == 0 || N == 0) return ok();
+    if ((R + 3) / 4 > 0x7fffffffLL || (N + 31) / 32 > 65535)
+        return fail(MWC_ERR_UNSUPPORTED, "scan shape too large");
+    LinArgs la{};
+    la.a = a; la.h = h; la.g = g; la.ga = ga; la.gx = gx; la.R = R; la.L = L; la.N = N;
+    la.vec = 0;
+    cudaError_t e = launch_lin_bwd(la, dtype, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "linear scan backward launch");
+    return ok();
+}
+
+}  // extern "C"

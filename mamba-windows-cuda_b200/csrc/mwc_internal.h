@@ -1,0 +1,119 @@
+// Host-side launch interface between the C ABI (capi.cu) and the kernel files.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mwc {
+
+// Forward scan over one L-segment per blockIdx.z (segment length seg_len, a multiple
+// of the time tile). Segment 0 starts from h_prev (or 0), later segments from 0.
+struct FwdArgs {
+    const void* u;
+    const void* delta;
+    const void* A;
+    const void* Bm;
+    const void* Cm;
+    const void* Dv;
+    const void* h_prev;   // nullable
+    void* out;            // nullable (checkpoint-only recompute)
+    void* h_last;         // nullable; written only when nseg == 1
+    float* ckpt;          // nullable; (B, nck, D, 16)
+    float* decay;         // nullable; written only when nseg == 1
+    float* carry;         // (B, nseg, D, 17) when nseg > 1: local end state + sum of delta
+    int64_t B, L, D;
+    int64_t seg_len;
+    int nseg;
+    int nck;
+    int vec;              // 16-byte vector access of (.., D) rows is legal
+};
+
+// Carry fold + truncated fixup. mode 0: h_in for segment s = 1 + blockIdx.z is folded from
+// `carry`; mode 1: one segment over all of L with the explicit h_in / decay.
+struct FixupArgs {
+    const void* delta;
+    const void* A;
+    const void* Cm;
+    const float* carry;   // mode 0
+    const float* h_in;    // mode 1
+    const float* decay;   // mode 1 (needed for h_last)
+    void* out;            // nullable, read-modify-write
+    void* h_last;         // nullable
+    float* decay_out;     // nullable, mode 0: total decay of the call
+    float* ckpt;          // nullable, read-modify-write
+    int64_t B, L, D;
+    int64_t seg_len;
+    int nseg;
+    int nck;
+    int mode;
+    int vec;
+};
+
+struct BwdArgs {
+    const void* u;
+    const void* delta;
+    const void* A;
+    const void* Bm;
+    const void* Cm;
+    const void* Dv;
+    const void* h_prev;   // nullable
+    const void* dout;
+    const void* dh_last;  // nullable
+    const float* ckpt;    // required when nck > 1
+    void* du;
+    void* ddelta;
+    void* dh_prev;        // nullable
+    float* ws_bc;         // (nblk, B, nck*16, 32) per-CTA dB|dC partial sums
+    float* ws_a;          // (B, D, 16) per-batch dA partial sums
+    float* ws_d;          // (B, D) per-batch dD partial sums
+    int64_t B, L, D;
+    int nck;
+    int nblk;
+    int vec;
+};
+
+struct BwdFinalArgs {
+    const float* ws_bc;
+    const float* ws_a;
+    const float* ws_d;
+    void* dA;
+    void* dB;
+    void* dC;
+    void* dD;
+    int64_t B, L, D;
+    int nck;
+    int nblk;
+};
+
+struct LinArgs {
+    const void* a;
+    const void* x;     // fwd
+    const void* h;     // bwd: forward output
+    const void* g;     // bwd: upstream gradient
+    void* out_h;       // fwd output
+    void* ga;          // bwd outputs
+    void* gx;
+    int64_t R, L, N;
+    int vec;
+};
+
+// Launch-shape descriptors chosen by the host heuristics in capi.cu.
+struct FwdPlan {
+    int states_per_thread;  // 16, 8 or 4
+    int channels_per_block;
+    int nseg;
+    int64_t seg_len;
+};
+
+FwdPlan plan_fwd(int64_t B, int64_t L, int64_t D, int dtype, int num_sms);
+int64_t fwd_carry_floats(const FwdPlan& plan, int64_t B, int64_t D);
+int bwd_channels_per_block(int dtype);
+
+cudaError_t launch_fwd(const FwdArgs& a, const FwdPlan& plan, int dtype, cudaStream_t s);
+cudaError_t launch_fixup(const FixupArgs& a, const FwdPlan& plan, int dtype, cudaStream_t s);
+cudaError_t launch_bwd(const BwdArgs& a, int dtype, cudaStream_t s);
+cudaError_t launch_bwd_final(const BwdFinalArgs& a, int dtype, cudaStream_t s);
+cudaError_t launch_lin_fwd(const LinArgs& a, int dtype, cudaStream_t s);
+cudaError_t launch_lin_bwd(const LinArgs& a, int dtype, cudaStream_t s);
+
+}  // namespace mwc

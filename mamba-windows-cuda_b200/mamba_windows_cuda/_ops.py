@@ -1,0 +1,207 @@
+"""Tensor-level wrappers around the C ABI: validation, allocation, stream and device.
+
+Every tensor (outputs and workspaces) is allocated here with the PyTorch caching
+allocator and handed to libmwc_b200.so as a raw pointer together with
+``torch.cuda.current_stream()``; the library itself allocates nothing.
+
+Validation mirrors the reference's host checks (mamba_windows_cuda/mamba_cuda.py:186-238)
+and raises RuntimeError with the same messages.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+NSTATE = 16
+CK = 16
+
+_DTYPES = {torch.float32: _lib.MWC_F32, torch.float16: _lib.MWC_F16}
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError:
+        raise RuntimeError("u must be float32/float16") from None
+
+
+def _p(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def check_ss_inputs(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=None):
+    """The reference's TORCH_CHECKs for the selective-scan forward (mamba_cuda.py:186-238)."""
+    named = (("u", u), ("delta", delta), ("A", A), ("B_ssm", B_ssm), ("C_ssm", C_ssm),
+             ("D_ssm", D_ssm))
+    for name, t in named:
+        if not isinstance(t, torch.Tensor) or not t.is_cuda:
+            raise RuntimeError(f"{name} must be a CUDA tensor")
+    if u.dtype not in _DTYPES:
+        raise RuntimeError("u must be float32/float16")
+    for name, t in named[1:]:
+        if t.dtype != u.dtype:
+            raise RuntimeError(f"{name} dtype must match u dtype")
+    if u.dim() != 3:
+        raise RuntimeError("u must be 3D (batch, seqlen, dim)")
+    if A.dim() != 2:
+        raise RuntimeError("A must be 2D (dim, state)")
+    Bb, L, D = u.shape
+    N = A.size(1)
+    if N != NSTATE:
+        raise RuntimeError("Only N=16 is supported")
+    if delta.dim() != 3:
+        raise RuntimeError("delta must be 3D (batch, seqlen, dim)")
+    if B_ssm.dim() != 3:
+        raise RuntimeError("B_ssm must be 3D (batch, seqlen, state)")
+    if C_ssm.dim() != 3:
+        raise RuntimeError("C_ssm must be 3D (batch, seqlen, state)")
+    if D_ssm.dim() != 1:
+        raise RuntimeError("D_ssm must be 1D (dim)")
+    if tuple(delta.shape) != (Bb, L, D):
+        raise RuntimeError("delta shape mismatch")
+    if tuple(A.shape) != (D, N):
+        raise RuntimeError("A shape mismatch")
+    if tuple(B_ssm.shape) != (Bb, L, N):
+        raise RuntimeError("B_ssm shape mismatch")
+    if tuple(C_ssm.shape) != (Bb, L, N):
+        raise RuntimeError("C_ssm shape mismatch")
+    if tuple(D_ssm.shape) != (D,):
+        raise RuntimeError("D_ssm shape mismatch")
+    if h_prev is not None:
+        if not isinstance(h_prev, torch.Tensor) or not h_prev.is_cuda:
+            raise RuntimeError("h_prev must be a CUDA tensor")
+        if h_prev.dtype != u.dtype:
+            raise RuntimeError("h_prev dtype must match u dtype")
+        if h_prev.dim() != 3:
+            raise RuntimeError("h_prev must be 3D (batch, dim, state)")
+        if tuple(h_prev.shape) != (Bb, D, N):
+            raise RuntimeError("h_prev shape must be (B, D, N)")
+    dev = u.device
+    for name, t in named + (("h_prev", h_prev),):
+        if t is not None and t.device != dev:
+            raise RuntimeError(f"{name} must be on the same device as u")
+
+
+def ckpt_count(L: int) -> int:
+    return (L + CK - 1) // CK
+
+
+def ss_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=None, *, want_out=True,
+               want_h_last=False, want_ckpt=False, want_decay=False):
+    """Run the forward scan. Inputs must be contiguous and validated.
+
+    Returns (out, h_last, ckpt, decay); entries not requested are None.
+    """
+    Bb, L, D = u.shape
+    dev = u.device
+    out = torch.empty_like(u) if want_out else None
+    h_last = torch.empty((Bb, D, NSTATE), dtype=u.dtype, device=dev) if want_h_last else None
+    ckpt = (torch.empty((Bb, ckpt_count(L), D, NSTATE), dtype=torch.float32, device=dev)
+            if want_ckpt else None)
+    decay = (torch.empty((Bb, D, NSTATE), dtype=torch.float32, device=dev)
+             if want_decay else None)
+    if L == 0 or Bb == 0 or D == 0:
+        if h_last is not None:
+            h_last.copy_(h_prev) if h_prev is not None else h_last.zero_()
+        if decay is not None:
+            decay.fill_(1.0)
+        return out, h_last, ckpt, decay
+    lib = _lib.load()
+    dt = dtype_code(u)
+    with torch.cuda.device(dev):
+        ws_bytes = int(lib.mwc_ss_fwd_workspace_bytes(Bb, L, D, dt))
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes > 0 else None
+        rc = lib.mwc_ss_fwd(_p(u), _p(delta), _p(A), _p(B_ssm), _p(C_ssm), _p(D_ssm),
+                            _p(h_prev), _p(out), _p(h_last), _p(ckpt), _p(decay), _p(ws),
+                            ws_bytes, Bb, L, D, dt, _stream(dev))
+    _lib.check(rc, "selective_scan forward")
+    return out, h_last, ckpt, decay
+
+
+def ss_backward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev, dout, dh_last, ckpt,
+                want_dh_prev=False):
+    """Reverse scan. dout (B,L,D) and dh_last (B,D,16) may be None (zero).
+
+    Returns (du, ddelta, dA, dB, dC, dD, dh_prev) in the input dtype.
+    """
+    Bb, L, D = u.shape
+    dev = u.device
+    if dout is None:
+        dout = torch.zeros_like(u)
+    du = torch.empty_like(u)
+    ddelta = torch.empty_like(delta)
+    dA = torch.empty_like(A)
+    dB = torch.empty_like(B_ssm)
+    dC = torch.empty_like(C_ssm)
+    dD = torch.empty_like(D_ssm)
+    dh_prev = torch.empty((Bb, D, NSTATE), dtype=u.dtype, device=dev) if want_dh_prev else None
+    if L == 0 or Bb == 0 or D == 0:
+        for t in (du, ddelta, dA, dB, dC, dD):
+            t.zero_()
+        if dh_prev is not None:
+            dh_prev.copy_(dh_last) if dh_last is not None else dh_prev.zero_()
+        return du, ddelta, dA, dB, dC, dD, dh_prev
+    lib = _lib.load()
+    dt = dtype_code(u)
+    with torch.cuda.device(dev):
+        ws_bytes = int(lib.mwc_ss_bwd_workspace_bytes(Bb, L, D, dt))
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        rc = lib.mwc_ss_bwd(_p(u), _p(delta), _p(A), _p(B_ssm), _p(C_ssm), _p(D_ssm),
+                            _p(h_prev), _p(dout), _p(dh_last), _p(ckpt), _p(du), _p(ddelta),
+                            _p(dA), _p(dB), _p(dC), _p(dD), _p(dh_prev), _p(ws), ws_bytes,
+                            Bb, L, D, dt, _stream(dev))
+    _lib.check(rc, "selective_scan backward")
+    return du, ddelta, dA, dB, dC, dD, dh_prev
+
+
+def ss_fixup(delta, A, C_ssm, h_in, decay=None, out=None, h_last=None, ckpt=None):
+    """Fold an incoming float32 state h_in (B, D, 16) into a scan run from zero, in place."""
+    Bb, L, D = delta.shape
+    if L == 0 or Bb == 0 or D == 0:
+        if h_last is not None and decay is not None:
+            h_last.copy_((decay * h_in + h_last.float()).to(h_last.dtype))
+        return
+    lib = _lib.load()
+    dt = dtype_code(delta)
+    dev = delta.device
+    with torch.cuda.device(dev):
+        rc = lib.mwc_ss_fixup(_p(delta), _p(A), _p(C_ssm), _p(h_in), _p(decay), _p(out),
+                              _p(h_last), _p(ckpt), Bb, L, D, dt, _stream(dev))
+    _lib.check(rc, "selective_scan fixup")
+
+
+def lin_scan_forward(a, x):
+    """h_0 = x_0, h_t = a_t h_{t-1} + x_t along dim 2 of contiguous (B, D, L, N) tensors."""
+    Bb, Dd, L, N = x.shape
+    h = torch.empty_like(x)
+    if h.numel() == 0:
+        return h
+    lib = _lib.load()
+    dev = x.device
+    with torch.cuda.device(dev):
+        rc = lib.mwc_lin_scan_fwd(_p(a), _p(x), _p(h), Bb * Dd, L, N, dtype_code(x),
+                                  _stream(dev))
+    _lib.check(rc, "parallel_scan forward")
+    return h
+
+
+def lin_scan_backward(a, h, g):
+    Bb, Dd, L, N = g.shape
+    ga = torch.empty_like(g)
+    gx = torch.empty_like(g)
+    if g.numel() == 0:
+        return ga, gx
+    lib = _lib.load()
+    dev = g.device
+    with torch.cuda.device(dev):
+        rc = lib.mwc_lin_scan_bwd(_p(a), _p(h), _p(g), _p(ga), _p(gx), Bb * Dd, L, N,
+                                  dtype_code(g), _stream(dev))
+    _lib.check(rc, "parallel_scan backward")
+    return ga, gx

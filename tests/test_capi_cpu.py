@@ -1,0 +1,121 @@
+"""CPU-only checks of the native boundary and the host logic (no GPU compute).
+
+* libmwc_b200.so loads and exports every entry point include/mwc_b200.h declares;
+* host-side validation returns the documented status codes before touching the GPU;
+* the Python API raises RuntimeError like the reference's TORCH_CHECKs;
+* the plain-PyTorch API functions kept from the reference (selective_scan_ref,
+  selective_scan_backward, parallel_scan_ref) agree with the oracle.
+"""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+import torch
+
+from _helpers import make_inputs, np64, rel_err
+from oracle import oracle as O
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "mwc_b200.h")
+
+
+def header_functions():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"MWC_API\s+[\w\s\*]+?\b(mwc_\w+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from mamba_windows_cuda import _lib
+    return _lib.load()
+
+
+def test_library_exports_every_header_symbol(lib):
+    from mamba_windows_cuda import _lib
+    names = header_functions()
+    assert len(names) >= 11
+    raw = ctypes.CDLL(_lib.LIB_PATH)
+    for n in names:
+        assert hasattr(raw, n), f"{n} missing from {_lib.LIB_NAME}"
+    assert set(names) == set(_lib.SIGNATURES), "ctypes signatures out of sync with the header"
+
+
+def test_library_identity(lib):
+    assert lib.mwc_abi_version() == 1
+    assert b"sm_100a" in lib.mwc_build_info()
+
+
+def test_size_queries(lib):
+    assert lib.mwc_ss_ckpt_count(1) == 1
+    assert lib.mwc_ss_ckpt_count(16) == 1
+    assert lib.mwc_ss_ckpt_count(17) == 2
+    assert lib.mwc_ss_ckpt_count(0) == 0
+    ws = lib.mwc_ss_bwd_workspace_bytes(4, 2048, 5120, 1)
+    assert ws > 4 * 5120 * 17 * 4 and ws % 256 == 0
+    # a long sequence with few channels is scanned in segments and needs carry space
+    assert lib.mwc_ss_fwd_workspace_bytes(1, 65536, 2048, 0) > 0
+    assert lib.mwc_ss_fwd_workspace_bytes(4, 2048, 5120, 1) == 0
+
+
+def test_c_abi_rejects_bad_arguments_without_touching_the_gpu(lib):
+    nul = None
+    fake = ctypes.c_void_p(16)  # never dereferenced: validation fails first
+    rc = lib.mwc_ss_fwd(fake, fake, fake, fake, fake, fake, nul, fake, nul, nul, nul, nul, 0,
+                        1, 16, 16, 7, nul)
+    assert rc == 1 and b"float32/float16" in lib.mwc_last_error()
+    rc = lib.mwc_ss_fwd(nul, fake, fake, fake, fake, fake, nul, fake, nul, nul, nul, nul, 0,
+                        1, 16, 16, 0, nul)
+    assert rc == 1 and b"required" in lib.mwc_last_error()
+    rc = lib.mwc_ss_fwd(fake, fake, fake, fake, fake, fake, nul, nul, nul, nul, nul, nul, 0,
+                        1, 16, 16, 0, nul)
+    assert rc == 1 and b"no output" in lib.mwc_last_error()
+    rc = lib.mwc_ss_fwd(fake, fake, fake, fake, fake, fake, nul, fake, nul, nul, nul, nul, 0,
+                        1, 0, 16, 0, nul)
+    assert rc == 1 and b"empty" in lib.mwc_last_error()
+    rc = lib.mwc_ss_bwd(*([fake] * 6), nul, fake, nul, nul, *([fake] * 6), nul, fake, 1 << 40,
+                        1, 64, 16, 0, nul)
+    assert rc == 1 and b"checkpoint" in lib.mwc_last_error()
+    rc = lib.mwc_ss_bwd(*([fake] * 6), nul, fake, nul, fake, *([fake] * 6), nul, fake, 8,
+                        1, 64, 16, 0, nul)
+    assert rc == 3 and b"workspace" in lib.mwc_last_error()
+    rc = lib.mwc_ss_fixup(fake, fake, nul, fake, nul, fake, nul, nul, 1, 16, 16, 0, nul)
+    assert rc == 1 and b"C_ssm" in lib.mwc_last_error()
+    rc = lib.mwc_lin_scan_fwd(fake, nul, fake, 1, 16, 1, 0, nul)
+    assert rc == 1
+
+
+def test_python_api_rejects_cpu_tensors_like_the_reference():
+    import mamba_windows_cuda as m
+    x = make_inputs(1, 8, 4)
+    with pytest.raises(RuntimeError, match="must be a CUDA tensor"):
+        m.SelectiveScanCuda()(x["u"], x["delta"], x["A"], x["Bm"], x["Cm"], x["Dv"])
+    with pytest.raises(RuntimeError, match="must be a CUDA tensor"):
+        m.SelectiveScanCuda().forward_with_state(x["u"], x["delta"], x["A"], x["Bm"], x["Cm"],
+                                                 x["Dv"])
+    with pytest.raises(RuntimeError, match="must be a CUDA tensor"):
+        m.parallel_scan_fn(torch.rand(1, 2, 8, 1), torch.rand(1, 2, 8, 1))
+
+
+def test_selective_scan_ref_and_backward_match_oracle():
+    from mamba_windows_cuda.mamba_cuda import selective_scan_backward, selective_scan_ref
+    x = make_inputs(2, 40, 12, torch.float64, seed=4, with_state=True)
+    out, h_last, inter = selective_scan_ref(x["u"], x["delta"], x["A"], x["Bm"], x["Cm"], x["Dv"],
+                                            x["h_prev"], return_intermediates=True)
+    ref_out, ref_h = O.ss_fwd(*[np64(x[k]) for k in ("u", "delta", "A", "Bm", "Cm", "Dv")],
+                              np64(x["h_prev"]))
+    assert rel_err(out, ref_out) < 1e-12 and rel_err(h_last, ref_h) < 1e-12
+    g = selective_scan_backward(x["g"], x["gh"], inter, x["Dv"])
+    ref = O.ss_bwd(*[np64(x[k]) for k in ("u", "delta", "A", "Bm", "Cm", "Dv")], np64(x["g"]),
+                   np64(x["h_prev"]), np64(x["gh"]))
+    for got, k in zip(g, ("du", "ddelta", "dA", "dB", "dC", "dD", "dh_prev")):
+        assert rel_err(got, ref[k]) < 1e-10, k
+
+
+def test_parallel_scan_ref_matches_oracle():
+    from mamba_windows_cuda import parallel_scan_ref
+    g = torch.Generator().manual_seed(0)
+    A = torch.rand(2, 3, 50, 4, generator=g, dtype=torch.float64)
+    X = torch.randn(2, 3, 50, 4, generator=g, dtype=torch.float64)
+    assert rel_err(parallel_scan_ref(A, X), O.lin_fwd(A, X)) < 1e-14
