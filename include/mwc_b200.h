@@ -58,8 +58,9 @@ MWC_API const char* mwc_build_info(void);            /* compiler / arch string o
 /* Number of float32 checkpoint states per channel for a sequence of length L (ceil(L/16)). */
 MWC_API int64_t mwc_ss_ckpt_count(int64_t L);
 
-/* Workspace bytes mwc_ss_fwd needs for (B, L, D) on the current device (0 when the
- * whole sequence is scanned by one pass; > 0 when it is split along L). */
+/* Workspace bytes mwc_ss_fwd needs for (B, L, D) on the current device: segment carries
+ * when the sequence is split along L, or the work-queue flags and segment hand-off states
+ * of the persistent kernel when B*D/128 reaches the SM count; 0 for a single pass. */
 MWC_API int64_t mwc_ss_fwd_workspace_bytes(int64_t B, int64_t L, int64_t D, int dtype);
 
 /*

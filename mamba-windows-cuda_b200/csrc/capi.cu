@@ -10,6 +10,8 @@
 #include <cstdint>
 #include <cstdio>
 
+#include <algorithm>
+
 #include "mwc_b200.h"
 #include "mwc_device.cuh"
 #include "mwc_internal.h"
@@ -108,8 +110,12 @@ int64_t mwc_ss_ckpt_count(int64_t L) { return L <= 0 ? 0 : (L + CK - 1) / CK; }
 
 int64_t mwc_ss_fwd_workspace_bytes(int64_t B, int64_t L, int64_t D, int dtype) {
     if (B <= 0 || L <= 0 || D <= 0) return 0;
-    const FwdPlan plan = plan_fwd(B, L, D, dtype, device_sms());
-    return align_up(fwd_carry_floats(plan, B, D) * 4, 256);
+    const int sms = device_sms();
+    const FwdPlan plan = plan_fwd(B, L, D, dtype, sms);
+    int64_t need = align_up(fwd_carry_floats(plan, B, D) * 4, 256);
+    const PersistPlan pp = plan_persistent(B, L, D, sms);
+    if (pp.ok) need = std::max<int64_t>(need, align_up(persistent_ws_bytes(pp), 256));
+    return need;
 }
 
 int mwc_ss_fwd(const void* u, const void* delta, const void* A, const void* Bm, const void* Cm,
@@ -124,7 +130,38 @@ int mwc_ss_fwd(const void* u, const void* delta, const void* A, const void* Bm, 
     if (!out && !h_last && !ckpt && !decay)
         return fail(MWC_ERR_INVALID, "no output requested");
     if (B == 0 || D == 0) return ok();
-    const FwdPlan plan = plan_fwd(B, L, D, dtype, device_sms());
+    const int sms = device_sms();
+    const size_t es0 = elem_size(dtype);
+    const PersistPlan pp = plan_persistent(B, L, D, sms);
+    const bool tma_ok = pp.ok && ((D * (int64_t)es0) % 16 == 0) && aligned16(u) &&
+                        aligned16(delta) && aligned16(Bm) && aligned16(Cm) &&
+                        (!out || aligned16(out)) && L <= 0x7fffffffLL && D <= 0x7fffffffLL;
+    if (tma_ok) {
+        const int64_t pneed = align_up(persistent_ws_bytes(pp), 256);
+        if (!workspace || workspace_bytes < pneed)
+            return fail(MWC_ERR_WORKSPACE, "forward workspace of %lld bytes required, got %lld",
+                        (long long)pneed, (long long)workspace_bytes);
+        if (!aligned16(workspace))
+            return fail(MWC_ERR_WORKSPACE, "forward workspace must be 16-byte aligned");
+        PFwdArgs pa{};
+        bool maps = make_tmap_3d(&pa.tm_u, u, dtype, D, L, B, 128, 32) &&
+                    make_tmap_3d(&pa.tm_d, delta, dtype, D, L, B, 128, 32) &&
+                    make_tmap_3d(&pa.tm_B, Bm, dtype, NSTATE, L, B, NSTATE, 32) &&
+                    make_tmap_3d(&pa.tm_C, Cm, dtype, NSTATE, L, B, NSTATE, 32) &&
+                    make_tmap_3d(&pa.tm_y, out ? out : u, dtype, D, L, B, 128, 32);
+        if (maps) {
+            pa.A = A; pa.Dv = Dv; pa.h_prev = h_prev; pa.h_last = h_last;
+            pa.ckpt = ckpt; pa.decay = decay;
+            pa.B = (int)B; pa.L = (int)L; pa.D = (int)D;
+            pa.nck = (int)mwc_ss_ckpt_count(L);
+            pa.has_out = out != nullptr;
+            cudaError_t e = launch_fwd_persistent(pa, pp, dtype, workspace,
+                                                  static_cast<cudaStream_t>(stream));
+            if (e != cudaSuccess) return cuda_fail(e, "selective-scan persistent forward launch");
+            return ok();
+        }
+    }
+    const FwdPlan plan = plan_fwd(B, L, D, dtype, sms);
     const int64_t need = align_up(fwd_carry_floats(plan, B, D) * 4, 256);
     if (need > 0 && (!workspace || workspace_bytes < need))
         return fail(MWC_ERR_WORKSPACE, "forward workspace of %lld bytes required, got %lld",
@@ -156,7 +193,10 @@ int mwc_ss_fwd(const void* u, const void* delta, const void* A, const void* Bm, 
 
 int64_t mwc_ss_bwd_workspace_bytes(int64_t B, int64_t L, int64_t D, int dtype) {
     if (B <= 0 || L <= 0 || D <= 0) return 0;
-    return bwd_ws(B, L, D, dtype).total;
+    int64_t need = bwd_ws(B, L, D, dtype).total;
+    const PersistPlan pb = plan_persistent_bwd(B, L, D, device_sms());
+    if (pb.ok) need = std::max<int64_t>(need, bwd_persistent_ws(pb, B, L).total);
+    return need;
 }
 
 int mwc_ss_bwd(const void* u, const void* delta, const void* A, const void* Bm, const void* Cm,
@@ -175,6 +215,39 @@ int mwc_ss_bwd(const void* u, const void* delta, const void* A, const void* Bm, 
     if (nck > 1 && !ckpt)
         return fail(MWC_ERR_INVALID, "checkpoint states are required when L > %d", CK);
     if (B == 0 || D == 0) return ok();
+    {
+        const size_t es0 = elem_size(dtype);
+        const PersistPlan pb = plan_persistent_bwd(B, L, D, device_sms());
+        const bool tma_ok = pb.ok && ((D * (int64_t)es0) % 16 == 0) && aligned16(u) &&
+                            aligned16(delta) && aligned16(dout) && aligned16(Bm) &&
+                            aligned16(Cm) && aligned16(A) && aligned16(du) && aligned16(ddelta) &&
+                            (!ckpt || aligned16(ckpt)) && (!h_prev || aligned16(h_prev)) &&
+                            (!dh_last || aligned16(dh_last)) && (!dh_prev || aligned16(dh_prev)) &&
+                            L <= 0x7fffffffLL && D <= 0x7fffffffLL;
+        if (tma_ok) {
+            const BwdPersistWs pw = bwd_persistent_ws(pb, B, L);
+            if (!workspace || workspace_bytes < pw.total)
+                return fail(MWC_ERR_WORKSPACE, "backward workspace of %lld bytes required, got %lld",
+                            (long long)pw.total, (long long)workspace_bytes);
+            if (!aligned16(workspace))
+                return fail(MWC_ERR_WORKSPACE, "backward workspace must be 16-byte aligned");
+            PBwdArgs pa{};
+            const bool maps = make_tmap_3d(&pa.tm_u, u, dtype, D, L, B, 128, CK) &&
+                              make_tmap_3d(&pa.tm_d, delta, dtype, D, L, B, 128, CK) &&
+                              make_tmap_3d(&pa.tm_g, dout, dtype, D, L, B, 128, CK) &&
+                              make_tmap_3d(&pa.tm_B, Bm, dtype, NSTATE, L, B, NSTATE, CK) &&
+                              make_tmap_3d(&pa.tm_C, Cm, dtype, NSTATE, L, B, NSTATE, CK);
+            if (maps) {
+                pa.A = A; pa.Dv = Dv; pa.h_prev = h_prev; pa.dh_last = dh_last; pa.ckpt = ckpt;
+                pa.du = du; pa.ddelta = ddelta; pa.dh_prev = dh_prev;
+                pa.B = (int)B; pa.L = (int)L; pa.D = (int)D; pa.nck = (int)nck;
+                cudaError_t e = launch_bwd_persistent(pa, pb, dtype, workspace, dA, dB, dC, dD,
+                                                      static_cast<cudaStream_t>(stream));
+                if (e != cudaSuccess) return cuda_fail(e, "selective-scan persistent backward launch");
+                return ok();
+            }
+        }
+    }
     const BwdWs w = bwd_ws(B, L, D, dtype);
     if (!workspace || workspace_bytes < w.total)
         return fail(MWC_ERR_WORKSPACE, "backward workspace of %lld bytes required, got %lld",

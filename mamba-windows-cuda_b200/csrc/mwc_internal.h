@@ -1,6 +1,7 @@
 // Host-side launch interface between the C ABI (capi.cu) and the kernel files.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -96,6 +97,67 @@ struct LinArgs {
     int64_t R, L, N;
     int vec;
 };
+
+// Persistent TMA forward (ss_fwd_tma.cu). Tensor maps are 3-D (inner, L, B) views.
+struct PFwdArgs {
+    CUtensorMap tm_u, tm_d, tm_B, tm_C, tm_y;
+    const void* A;
+    const void* Dv;
+    const void* h_prev;
+    void* h_last;
+    float* ckpt;
+    float* decay;
+    float* hand;     // (chains, K, 128, 17): state + sum(delta) handed to the next segment
+    int* flags;      // (chains, K) segment-done flags
+    int* counter;    // unit queue head
+    int* err;        // bounded-wait error word
+    int B, L, D;
+    int nblk, nchains, K, seg_tiles, ntiles, nck;
+    int has_out;
+};
+
+struct PersistPlan {
+    bool ok;        // enough chains (>= SMs) for the queue to keep every SM busy
+    int nblk, nchains, ntiles, K, seg_tiles, grid;
+};
+
+PersistPlan plan_persistent(int64_t B, int64_t L, int64_t D, int num_sms);
+int64_t persistent_ws_bytes(const PersistPlan& pl);
+bool make_tmap_3d(CUtensorMap* map, const void* base, int dtype, int64_t W, int64_t L, int64_t B,
+                  int bw, int bl);
+cudaError_t launch_fwd_persistent(PFwdArgs& a, const PersistPlan& pl, int dtype, void* ws,
+                                  cudaStream_t s);
+
+// Persistent TMA backward (ss_bwd_tma.cu).
+struct PBwdArgs {
+    CUtensorMap tm_u, tm_d, tm_g, tm_B, tm_C;
+    const void* A;
+    const void* Dv;
+    const void* h_prev;
+    const void* dh_last;
+    const float* ckpt;
+    void* du;
+    void* ddelta;
+    void* dh_prev;
+    float* hand;     // (chains, K, 128, 16): adjoint state handed to the previous segment
+    float* ws_a;     // (units, 128, 16) dA partial sums
+    float* ws_d;     // (units, 128) dD partial sums
+    float* ws_bc;    // (blocks, B, nck*16, 32) dB | dC partial sums
+    int* flags;
+    int* counter;
+    int* err;
+    int B, L, D;
+    int nblk, nchains, K, seg_tiles, ntiles, nck;
+};
+
+struct BwdPersistWs {
+    int64_t off_hand, off_a, off_d, off_bc, total;
+};
+
+PersistPlan plan_persistent_bwd(int64_t B, int64_t L, int64_t D, int num_sms);
+BwdPersistWs bwd_persistent_ws(const PersistPlan& pl, int64_t B, int64_t L);
+cudaError_t launch_bwd_persistent(PBwdArgs& a, const PersistPlan& pl, int dtype, void* ws,
+                                  void* dA, void* dB, void* dC, void* dD, cudaStream_t s);
 
 // Launch-shape descriptors chosen by the host heuristics in capi.cu.
 struct FwdPlan {

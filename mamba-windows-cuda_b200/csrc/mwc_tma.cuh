@@ -1,0 +1,107 @@
+// TMA (cp.async.bulk.tensor), mbarrier and work-queue helpers for the persistent
+// sm_100a kernels. Every wait is bounded: on expiry the kernel records an error code in
+// global memory and the caller's wait returns false instead of spinning forever.
+#pragma once
+
+#include <cuda.h>
+#include <stdint.h>
+
+namespace mwc {
+
+// Error codes written to the workspace error word.
+constexpr int ERR_WAIT_TMA = 1;     // a TMA tile never arrived
+constexpr int ERR_WAIT_CHAIN = 2;   // the previous segment of a chain never published its state
+constexpr unsigned WAIT_SPINS = 1u << 24;   // a few seconds with the backoff below
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned phase) {
+    unsigned ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(phase)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for an mbarrier phase; records ERR_WAIT_TMA and returns false on expiry.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned phase, int* err) {
+    for (unsigned it = 0; it < WAIT_SPINS; ++it) {
+        if (mbar_try_wait(bar, phase)) return true;
+        if (it > 64) __nanosleep(32);
+    }
+    if (err) atomicCAS(err, 0, ERR_WAIT_TMA);
+    return false;
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int c1, int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0,
+                                             int c1, int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// Release / acquire flags used to hand a chain's state from one segment to the next.
+__device__ __forceinline__ void flag_release(int* f, int v) {
+    asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
+}
+__device__ __forceinline__ int flag_acquire(const int* f) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+    return v;
+}
+
+// Bounded wait until *f == v; records ERR_WAIT_CHAIN and returns false on expiry.
+__device__ __forceinline__ bool flag_wait(const int* f, int v, int* err) {
+    for (unsigned it = 0; it < WAIT_SPINS; ++it) {
+        if (flag_acquire(f) == v) return true;
+        __nanosleep(it < 64 ? 20 : 200);
+    }
+    if (err) atomicCAS(err, 0, ERR_WAIT_CHAIN);
+    return false;
+}
+
+}  // namespace mwc

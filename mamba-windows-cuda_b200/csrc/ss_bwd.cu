@@ -165,8 +165,7 @@ __global__ void __launch_bounds__(NW * 32) ss_bwd_kernel(const BwdArgs p) {
                 const float a = ex2(clampy ? fminf(x, ARG2_HI) : x);
                 const float g = fmaf(gy, sC[i][n], q[j]);
                 const float hprev = (i > 0) ? hc[i - 1][j] : h0[j];
-                float pp = g * (a * hprev);
-                if (clampy && !(x < ARG2_HI)) pp = 0.f;  // clamped exponent: no derivative
+                const float pp = g * (a * hprev);
                 s1 = fmaf(A2[j], pp, s1);
                 dA[j] = fmaf(dt, pp, dA[j]);
                 s2 = fmaf(g, sB[i][n], s2);

@@ -1,0 +1,556 @@
+// Persistent, TMA-pipelined backward selective scan for sm_100a.
+//
+// Same work decomposition as the persistent forward (chains of 128 channels of one batch
+// row, cut into K time segments, taken from an atomic queue), walked in reverse: the unit
+// for the last time segment of a chain starts from dh_last, every other unit waits for the
+// adjoint state q its successor segment published (release/acquire, bounded wait).
+//
+// Per 16-step tile (= one checkpoint chunk), processed last tile first:
+//   * TMA brings u, delta, dout (16 x 128), B, C (16 x 16) and, by a 1-D bulk copy, the
+//     float32 checkpoint state at the chunk start (128 x 16) into a 2-stage mbarrier ring;
+//   * the chunk's 16 states per (channel, state) are recomputed forward and kept in a
+//     per-thread shared-memory cache (conflict-free float4 layout);
+//   * the adjoint recurrence runs backwards through the chunk:
+//       g = dout C + q,  p = g a h_{t-1},  ddelta = ln2 <A2, p> + u <g, B>,
+//       du = dout D + delta <g, B>,  dA += delta p,  q = a g,
+//       dB_t = sum_d g delta u,  dC_t = sum_d dout h_t.
+// Thread layout: lane = (channel group cg, state group sg); a thread owns 4 adjacent
+// channels x 4 states, so the cross-channel sums of dB / dC start as in-thread FMAs and
+// finish with a 3-level butterfly over the 8 channel groups of the warp; the per-channel
+// sums <.,.> over states take 2 shuffle levels over the 4 state groups.
+// Every reduction has a fixed order (warp butterfly, warps in order, then the finalize
+// kernel over CTAs / segments / batch in order): results are bitwise reproducible.
+#include "mwc_device.cuh"
+#include "mwc_internal.h"
+#include "mwc_tma.cuh"
+
+#include <algorithm>
+
+namespace mwc {
+
+constexpr int PB_LT = CK;     // 16 steps per tile
+constexpr int PB_CPB = 128;
+constexpr int PB_NT = 128;
+constexpr int PB_ST = 2;
+
+template <typename T>
+struct __align__(1024) PBwdSmem {
+    float4 hc[PB_LT][4][PB_NT];                 // state cache: [step][channel c][thread]
+    float h0[PB_ST][PB_CPB][NSTATE];            // checkpoint at the chunk start
+    T u[PB_ST][PB_LT][PB_CPB];
+    T d[PB_ST][PB_LT][PB_CPB];
+    T g[PB_ST][PB_LT][PB_CPB];
+    T Bt[PB_ST][PB_LT][NSTATE];
+    T Ct[PB_ST][PB_LT][NSTATE];
+    float red[2][PB_NT / 32][PB_LT][2 * NSTATE];  // per-warp dB | dC partials, double buffered
+    float Bf[sizeof(T) == 2 ? PB_NT / 32 : 1][PB_LT][NSTATE];
+    float Cf[sizeof(T) == 2 ? PB_NT / 32 : 1][PB_LT][NSTATE];
+    uint64_t full[PB_ST];
+    int unit[PB_ST];
+    int tile[PB_ST];
+};
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+template <typename T>
+__device__ __forceinline__ void load4(float (&v)[4], const T* p);
+template <>
+__device__ __forceinline__ void load4<float>(float (&v)[4], const float* p) {
+    const float4 x = *reinterpret_cast<const float4*>(p);
+    v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+}
+template <>
+__device__ __forceinline__ void load4<__half>(float (&v)[4], const __half* p) {
+    const uint2 raw = *reinterpret_cast<const uint2*>(p);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+    v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+}
+
+template <typename T>
+__device__ __forceinline__ void store4(T* p, const float (&v)[4]);
+template <>
+__device__ __forceinline__ void store4<float>(float* p, const float (&v)[4]) {
+    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+}
+template <>
+__device__ __forceinline__ void store4<__half>(__half* p, const float (&v)[4]) {
+    __half2 a = __floats2half2_rn(v[0], v[1]);
+    __half2 b = __floats2half2_rn(v[2], v[3]);
+    uint2 raw;
+    raw.x = *reinterpret_cast<uint32_t*>(&a);
+    raw.y = *reinterpret_cast<uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(p) = raw;
+}
+
+__device__ __forceinline__ float2 f2(float x) { return make_float2(x, x); }
+
+__device__ __forceinline__ float2 ex2_clamped(float2 x) {
+    return make_float2(ex2(fminf(x.x, ARG2_HI)), ex2(fminf(x.y, ARG2_HI)));
+}
+
+template <typename T>
+__global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __grid_constant__ PBwdArgs p) {
+    extern __shared__ uint8_t smem_raw[];
+    PBwdSmem<T>& s = *reinterpret_cast<PBwdSmem<T>*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    constexpr bool HALF = sizeof(T) == 2;
+    const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
+    const int cg = lane >> 2, sg = lane & 3;
+    const int c4 = w * 32 + cg * 4;          // first of the thread's 4 channels in the block
+    const int total = p.nchains * p.K;
+    const int64_t Lp = (int64_t)p.nck * CK;
+    const unsigned tile_bytes = (unsigned)((3 * PB_LT * PB_CPB + 2 * PB_LT * NSTATE) * sizeof(T));
+
+    // ---- producer (thread 0) -------------------------------------------------------
+    int pu = -1, pcount = 0, ptiles = 0, pfirst = 0;
+    bool pdone = false;
+    auto issue = [&](int st) {
+        if (!pdone && (pu < 0 || pcount == ptiles)) {
+            pu = atomicAdd(p.counter, 1);
+            if (pu >= total) {
+                pdone = true;
+            } else {
+                const int k = p.K - 1 - pu / p.nchains;
+                pfirst = k * p.seg_tiles;
+                ptiles = min(p.seg_tiles, p.ntiles - pfirst);
+                pcount = 0;
+            }
+        }
+        if (pdone) {
+            s.unit[st] = -1;
+            return;
+        }
+        const int c = pu % p.nchains;
+        const int b = c / p.nblk, blk = c % p.nblk;
+        const int tix = pfirst + ptiles - 1 - pcount;
+        const int t0 = tix * PB_LT;
+        s.unit[st] = pu;
+        s.tile[st] = pcount;
+        const int nch = min(PB_CPB, p.D - blk * PB_CPB);
+        const unsigned hbytes = tix > 0 ? (unsigned)(nch * NSTATE * 4) : 0u;
+        mbar_expect_tx(&s.full[st], tile_bytes + hbytes);
+        tma_load_3d(&s.u[st][0][0], &p.tm_u, &s.full[st], blk * PB_CPB, t0, b);
+        tma_load_3d(&s.d[st][0][0], &p.tm_d, &s.full[st], blk * PB_CPB, t0, b);
+        tma_load_3d(&s.g[st][0][0], &p.tm_g, &s.full[st], blk * PB_CPB, t0, b);
+        tma_load_3d(&s.Bt[st][0][0], &p.tm_B, &s.full[st], 0, t0, b);
+        tma_load_3d(&s.Ct[st][0][0], &p.tm_C, &s.full[st], 0, t0, b);
+        if (tix > 0)
+            bulk_load(&s.h0[st][0][0],
+                      p.ckpt + (((int64_t)b * p.nck + tix - 1) * p.D + (int64_t)blk * PB_CPB) * NSTATE,
+                      hbytes, &s.full[st]);
+        ++pcount;
+    };
+
+    if (tid == 0) {
+        for (int st = 0; st < PB_ST; ++st) mbar_init(&s.full[st], 1);
+        fence_mbar_init();
+        prefetch_tmap(&p.tm_u);
+        prefetch_tmap(&p.tm_d);
+        prefetch_tmap(&p.tm_g);
+        prefetch_tmap(&p.tm_B);
+        prefetch_tmap(&p.tm_C);
+        for (int st = 0; st < PB_ST; ++st) issue(st);
+    }
+    __syncthreads();
+
+    const T* Ap = static_cast<const T*>(p.A);
+    const T* Dp = static_cast<const T*>(p.Dv);
+    float2 A2[4][2], q[4][2], dA[4][2];
+    float Dd[4], dD[4];
+    int64_t dbase = 0;                      // first of the 4 channels (global index)
+    int prev_blk = 0, prev_b = 0, prev_t0 = 0;
+
+    for (int it = 0;; ++it) {
+        const int st = it % PB_ST;
+        const unsigned phase = (unsigned)(it / PB_ST) & 1u;
+        const int unit = s.unit[st];
+
+        // dB | dC partials of the previous tile: sum the 4 warps in order, one row per step
+        if (it > 0) {
+            const int pb = (it - 1) & 1;
+            float* wb = p.ws_bc + (((int64_t)prev_blk * p.B + prev_b) * Lp + prev_t0) * (2 * NSTATE);
+#pragma unroll
+            for (int r = 0; r < (PB_LT * 2 * NSTATE) / PB_NT; ++r) {
+                const int idx = tid + r * PB_NT;
+                const int i = idx / (2 * NSTATE), v = idx % (2 * NSTATE);
+                wb[idx] = ((s.red[pb][0][i][v] + s.red[pb][1][i][v]) + s.red[pb][2][i][v]) +
+                          s.red[pb][3][i][v];
+            }
+        }
+        if (unit < 0) break;
+
+        const int pc = s.tile[st];
+        const int c = unit % p.nchains, kp = unit / p.nchains, k = p.K - 1 - kp;
+        const int b = c / p.nblk, blk = c % p.nblk;
+        const int first = k * p.seg_tiles;
+        const int ntl = min(p.seg_tiles, p.ntiles - first);
+        const int tix = first + ntl - 1 - pc;
+        const int t0 = tix * PB_LT;
+        const bool unit_end = pc == ntl - 1;
+        bool dvc[4];
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) dvc[cc] = (int64_t)blk * PB_CPB + c4 + cc < p.D;
+
+        if (pc == 0) {  // unit start
+            dbase = (int64_t)blk * PB_CPB + c4;
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+                float a4[4] = {0.f, 0.f, 0.f, 0.f};
+                if (dvc[cc]) load4<T>(a4, Ap + (dbase + cc) * NSTATE + 4 * sg);
+                A2[cc][0] = make_float2(a4[0] * LOG2E, a4[1] * LOG2E);
+                A2[cc][1] = make_float2(a4[2] * LOG2E, a4[3] * LOG2E);
+                Dd[cc] = dvc[cc] ? to_f(Dp[dbase + cc]) : 0.f;
+                dD[cc] = 0.f;
+                dA[cc][0] = dA[cc][1] = make_float2(0.f, 0.f);
+            }
+            if (kp == 0) {
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) {
+                    float g4[4] = {0.f, 0.f, 0.f, 0.f};
+                    if (p.dh_last != nullptr && dvc[cc])
+                        load4<T>(g4, static_cast<const T*>(p.dh_last) + ((int64_t)b * p.D + dbase + cc) * NSTATE + 4 * sg);
+                    q[cc][0] = make_float2(g4[0], g4[1]);
+                    q[cc][1] = make_float2(g4[2], g4[3]);
+                }
+            } else {
+                if (tid == 0) flag_wait(&p.flags[c * p.K + kp - 1], 1, p.err);
+                __syncthreads();
+                const float* hs = p.hand + ((int64_t)(c * p.K + kp - 1) * PB_CPB + c4) * NSTATE + 4 * sg;
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) {
+                    const float4 v = __ldcg(reinterpret_cast<const float4*>(hs + cc * NSTATE));
+                    q[cc][0] = make_float2(v.x, v.y);
+                    q[cc][1] = make_float2(v.z, v.w);
+                }
+            }
+        }
+
+        mbar_wait(&s.full[st], phase, p.err);
+        const float* Bf;
+        const float* Cf;
+        if constexpr (HALF) {
+            for (int idx = lane; idx < PB_LT * NSTATE; idx += 32) {
+                (&s.Bf[w][0][0])[idx] = to_f((&s.Bt[st][0][0])[idx]);
+                (&s.Cf[w][0][0])[idx] = to_f((&s.Ct[st][0][0])[idx]);
+            }
+            __syncwarp();
+            Bf = &s.Bf[w][0][0];
+            Cf = &s.Cf[w][0][0];
+        } else {
+            Bf = reinterpret_cast<const float*>(&s.Bt[st][0][0]);
+            Cf = reinterpret_cast<const float*>(&s.Ct[st][0][0]);
+        }
+
+        // state at the chunk start
+        float2 h[4][2];
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (tix > 0) {
+                v = *reinterpret_cast<const float4*>(&s.h0[st][c4 + cc][4 * sg]);
+            } else if (p.h_prev != nullptr && dvc[cc]) {
+                float hp4[4];
+                load4<T>(hp4, static_cast<const T*>(p.h_prev) + ((int64_t)b * p.D + dbase + cc) * NSTATE + 4 * sg);
+                v = make_float4(hp4[0], hp4[1], hp4[2], hp4[3]);
+            }
+            h[cc][0] = make_float2(v.x, v.y);
+            h[cc][1] = make_float2(v.z, v.w);
+        }
+        float2 h0[4][2];
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+            h0[cc][0] = h[cc][0];
+            h0[cc][1] = h[cc][1];
+        }
+
+        // ---- recompute the chunk's states -------------------------------------------
+#pragma unroll 2
+        for (int i = 0; i < PB_LT; ++i) {
+            float dt[4], uu[4];
+            load4<T>(dt, &s.d[st][i][c4]);
+            load4<T>(uu, &s.u[st][i][c4]);
+            const float4 B4 = *reinterpret_cast<const float4*>(Bf + i * NSTATE + 4 * sg);
+            const float2 Bp0 = make_float2(B4.x, B4.y), Bp1 = make_float2(B4.z, B4.w);
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+                const float2 dt2 = f2(dt[cc]);
+                const float2 du2 = f2(dt[cc] * uu[cc]);
+                const float2 a0 = ex2_clamped(__fmul2_rn(dt2, A2[cc][0]));
+                const float2 a1 = ex2_clamped(__fmul2_rn(dt2, A2[cc][1]));
+                h[cc][0] = __ffma2_rn(a0, h[cc][0], __fmul2_rn(du2, Bp0));
+                h[cc][1] = __ffma2_rn(a1, h[cc][1], __fmul2_rn(du2, Bp1));
+                s.hc[i][cc][tid] = make_float4(h[cc][0].x, h[cc][0].y, h[cc][1].x, h[cc][1].y);
+            }
+        }
+
+        // ---- adjoint pass -------------------------------------------------------------
+        T* dub = static_cast<T*>(p.du);
+        T* ddb = static_cast<T*>(p.ddelta);
+        float2 ht[4][2];
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+            ht[cc][0] = h[cc][0];
+            ht[cc][1] = h[cc][1];
+        }
+        const int oidx = (cg < 4) ? (4 * sg + cg) : (NSTATE + 4 * sg + cg - 4);
+#pragma unroll 1
+        for (int i = PB_LT - 1; i >= 0; --i) {
+            float dt[4], uu[4], gy[4];
+            load4<T>(dt, &s.d[st][i][c4]);
+            load4<T>(uu, &s.u[st][i][c4]);
+            load4<T>(gy, &s.g[st][i][c4]);
+            const float4 B4 = *reinterpret_cast<const float4*>(Bf + i * NSTATE + 4 * sg);
+            const float4 C4 = *reinterpret_cast<const float4*>(Cf + i * NSTATE + 4 * sg);
+            const float2 Bp[2] = {make_float2(B4.x, B4.y), make_float2(B4.z, B4.w)};
+            const float2 Cp[2] = {make_float2(C4.x, C4.y), make_float2(C4.z, C4.w)};
+            float2 hp[4][2];
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+                if (i > 0) {
+                    const float4 v = s.hc[i - 1][cc][tid];
+                    hp[cc][0] = make_float2(v.x, v.y);
+                    hp[cc][1] = make_float2(v.z, v.w);
+                } else {
+                    hp[cc][0] = h0[cc][0];
+                    hp[cc][1] = h0[cc][1];
+                }
+            }
+            float2 vB[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+            float2 vC[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+            float S1[4], S2[4];
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+                const float2 dt2 = f2(dt[cc]);
+                const float2 du2 = f2(dt[cc] * uu[cc]);
+                const float2 gy2 = f2(gy[cc]);
+                float2 s1 = make_float2(0.f, 0.f), s2 = make_float2(0.f, 0.f);
+#pragma unroll
+                for (int pr = 0; pr < 2; ++pr) {
+                    const float2 a = ex2_clamped(__fmul2_rn(dt2, A2[cc][pr]));
+                    const float2 g = __ffma2_rn(gy2, Cp[pr], q[cc][pr]);
+                    const float2 pp = __fmul2_rn(g, __fmul2_rn(a, hp[cc][pr]));
+                    s1 = __ffma2_rn(A2[cc][pr], pp, s1);
+                    dA[cc][pr] = __ffma2_rn(dt2, pp, dA[cc][pr]);
+                    s2 = __ffma2_rn(g, Bp[pr], s2);
+                    vB[pr] = __ffma2_rn(g, du2, vB[pr]);
+                    vC[pr] = __ffma2_rn(gy2, ht[cc][pr], vC[pr]);
+                    q[cc][pr] = __fmul2_rn(a, g);
+                }
+                S1[cc] = s1.x + s1.y;
+                S2[cc] = s2.x + s2.y;
+                dD[cc] = fmaf(gy[cc], uu[cc], dD[cc]);
+            }
+            // per-channel sums over the 4 state groups (xor 1, 2)
+#pragma unroll
+            for (int o = 1; o <= 2; o <<= 1) {
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) {
+                    S1[cc] += __shfl_xor_sync(FULL, S1[cc], o);
+                    S2[cc] += __shfl_xor_sync(FULL, S2[cc], o);
+                }
+            }
+            const int t = t0 + i;
+            if (sg == 0 && t < p.L) {
+                float duo[4], ddo[4];
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) {
+                    duo[cc] = fmaf(gy[cc], Dd[cc], dt[cc] * S2[cc]);
+                    ddo[cc] = fmaf(uu[cc], S2[cc], S1[cc] * LN2);
+                }
+                const int64_t off = ((int64_t)b * p.L + t) * p.D + dbase;
+                if (dvc[3]) {
+                    store4<T>(dub + off, duo);
+                    store4<T>(ddb + off, ddo);
+                } else {
+#pragma unroll
+                    for (int cc = 0; cc < 4; ++cc)
+                        if (dvc[cc]) {
+                            dub[off + cc] = from_f<T>(duo[cc]);
+                            ddb[off + cc] = from_f<T>(ddo[cc]);
+                        }
+                }
+            }
+            // dB | dC over the warp's 8 channel groups: reduce-scatter (xor 16, 8, 4)
+            float v[8] = {vB[0].x, vB[0].y, vB[1].x, vB[1].y, vC[0].x, vC[0].y, vC[1].x, vC[1].y};
+#pragma unroll
+            for (int m = 4; m >= 1; m >>= 1) {
+                const bool up = (cg & m) != 0;
+#pragma unroll
+                for (int j = 0; j < m; ++j) {
+                    const float send = up ? v[j] : v[j + m];
+                    const float keep = up ? v[j + m] : v[j];
+                    v[j] = keep + __shfl_xor_sync(FULL, send, m * 4);
+                }
+            }
+            s.red[it & 1][w][i][oidx] = v[0];
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+                ht[cc][0] = hp[cc][0];
+                ht[cc][1] = hp[cc][1];
+            }
+        }
+
+        if (unit_end) {
+            const int64_t ub = (int64_t)unit * PB_CPB + c4;
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc)
+                *reinterpret_cast<float4*>(p.ws_a + (ub + cc) * NSTATE + 4 * sg) =
+                    make_float4(dA[cc][0].x, dA[cc][0].y, dA[cc][1].x, dA[cc][1].y);
+            if (sg == 0)
+                *reinterpret_cast<float4*>(p.ws_d + ub) = make_float4(dD[0], dD[1], dD[2], dD[3]);
+            if (k > 0) {
+                float* hs = p.hand + ((int64_t)(c * p.K + kp) * PB_CPB + c4) * NSTATE + 4 * sg;
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc)
+                    *reinterpret_cast<float4*>(hs + cc * NSTATE) =
+                        make_float4(q[cc][0].x, q[cc][0].y, q[cc][1].x, q[cc][1].y);
+                __threadfence();
+            } else if (p.dh_prev != nullptr) {
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc)
+                    if (dvc[cc]) {
+                        const float v4[4] = {q[cc][0].x, q[cc][0].y, q[cc][1].x, q[cc][1].y};
+                        store4<T>(static_cast<T*>(p.dh_prev) + ((int64_t)b * p.D + dbase + cc) * NSTATE + 4 * sg, v4);
+                    }
+            }
+        }
+        prev_blk = blk;
+        prev_b = b;
+        prev_t0 = t0;
+        __syncthreads();
+        if (tid == 0) {
+            if (unit_end && k > 0) flag_release(&p.flags[c * p.K + kp], 1);
+            issue(st);
+        }
+    }
+}
+
+// Fixed-order sums of the persistent backward's partials into dA, dD (over batch rows and
+// segments) and dB, dC (over channel blocks).
+template <typename T>
+__global__ void ss_bwd_persistent_final_kernel(const __grid_constant__ PBwdArgs p, void* dA_,
+                                               void* dB_, void* dC_, void* dD_) {
+    const int64_t Lp = (int64_t)p.nck * CK;
+    const int64_t n_bc = (int64_t)p.B * p.L * 2 * NSTATE;
+    const int64_t n_a = (int64_t)p.D * NSTATE;
+    const int64_t total = n_bc + n_a + p.D;
+    T* dA = static_cast<T*>(dA_);
+    T* dB = static_cast<T*>(dB_);
+    T* dC = static_cast<T*>(dC_);
+    T* dD = static_cast<T*>(dD_);
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (int64_t)gridDim.x * blockDim.x) {
+        if (idx < n_bc) {
+            const int64_t v = idx % (2 * NSTATE);
+            const int64_t bt = idx / (2 * NSTATE);
+            const int64_t b = bt / p.L, t = bt % p.L;
+            float s = 0.f;
+            for (int blk = 0; blk < p.nblk; ++blk)
+                s += p.ws_bc[(((int64_t)blk * p.B + b) * Lp + t) * (2 * NSTATE) + v];
+            if (v < NSTATE) dB[bt * NSTATE + v] = from_f<T>(s);
+            else dC[bt * NSTATE + v - NSTATE] = from_f<T>(s);
+        } else {
+            const bool isA = idx < n_bc + n_a;
+            const int64_t i = isA ? idx - n_bc : idx - n_bc - n_a;
+            const int64_t d = isA ? i / NSTATE : i;
+            const int n = isA ? (int)(i % NSTATE) : 0;
+            const int blk = (int)(d / PB_CPB), ch = (int)(d % PB_CPB);
+            float s = 0.f;
+            for (int kp = 0; kp < p.K; ++kp)
+                for (int b = 0; b < p.B; ++b) {
+                    const int64_t unit = (int64_t)kp * p.nchains + b * p.nblk + blk;
+                    s += isA ? p.ws_a[(unit * PB_CPB + ch) * NSTATE + n] : p.ws_d[unit * PB_CPB + ch];
+                }
+            if (isA) dA[i] = from_f<T>(s);
+            else dD[i] = from_f<T>(s);
+        }
+    }
+}
+
+PersistPlan plan_persistent_bwd(int64_t B, int64_t L, int64_t D, int num_sms) {
+    PersistPlan pl{};
+    pl.nblk = (int)((D + PB_CPB - 1) / PB_CPB);
+    pl.nchains = (int)(B * pl.nblk);
+    pl.ntiles = (int)((L + PB_LT - 1) / PB_LT);
+    pl.ok = pl.nchains >= num_sms;
+    int best_k = 1;
+    double best = -1.0;
+    for (int K = 1; K <= pl.ntiles; ++K) {
+        const int seg = (pl.ntiles + K - 1) / K;
+        if ((pl.ntiles + seg - 1) / seg != K) continue;
+        if (K > 1 && seg < 4) break;
+        const int64_t U = (int64_t)pl.nchains * K;
+        const int64_t G = std::min<int64_t>(num_sms, U);
+        const int64_t waves = (U + G - 1) / G;
+        const double eff = (double)U / (double)(G * waves);
+        if (eff > best + 0.01) {
+            best = eff;
+            best_k = K;
+        }
+    }
+    pl.K = best_k;
+    pl.seg_tiles = (pl.ntiles + best_k - 1) / best_k;
+    pl.grid = (int)std::min<int64_t>(num_sms, (int64_t)pl.nchains * pl.K);
+    return pl;
+}
+
+// Workspace: [counter, err, flags | hand | ws_a | ws_d | ws_bc], 256-byte aligned parts.
+BwdPersistWs bwd_persistent_ws(const PersistPlan& pl, int64_t B, int64_t L) {
+    BwdPersistWs w{};
+    const int64_t units = (int64_t)pl.nchains * pl.K;
+    auto up = [](int64_t x) { return (x + 255) / 256 * 256; };
+    w.off_hand = up(16 + units * 4);
+    w.off_a = w.off_hand + up(units * PB_CPB * NSTATE * 4);
+    w.off_d = w.off_a + up(units * PB_CPB * NSTATE * 4);
+    w.off_bc = w.off_d + up(units * PB_CPB * 4);
+    const int64_t Lp = (L + CK - 1) / CK * CK;
+    w.total = w.off_bc + up((int64_t)pl.nblk * B * Lp * 2 * NSTATE * 4);
+    return w;
+}
+
+template <typename T>
+static cudaError_t launch_pb(const PBwdArgs& a, int grid, void* dA, void* dB, void* dC, void* dD,
+                             cudaStream_t s) {
+    const size_t smem = sizeof(PBwdSmem<T>) + 1024;
+    cudaError_t e = cudaFuncSetAttribute(ss_bwd_persistent_kernel<T>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    ss_bwd_persistent_kernel<T><<<grid, PB_NT, smem, s>>>(a);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    const int64_t total = (int64_t)a.B * a.L * 2 * NSTATE + (int64_t)a.D * NSTATE + a.D;
+    int64_t blocks = std::min<int64_t>((total + 255) / 256, 148 * 8);
+    ss_bwd_persistent_final_kernel<T><<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, s>>>(a, dA, dB, dC, dD);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_bwd_persistent(PBwdArgs& a, const PersistPlan& pl, int dtype, void* ws,
+                                  void* dA, void* dB, void* dC, void* dD, cudaStream_t s) {
+    const BwdPersistWs w = bwd_persistent_ws(pl, a.B, a.L);
+    char* base = static_cast<char*>(ws);
+    a.counter = reinterpret_cast<int*>(base);
+    a.err = reinterpret_cast<int*>(base + 4);
+    a.flags = reinterpret_cast<int*>(base + 16);
+    a.hand = reinterpret_cast<float*>(base + w.off_hand);
+    a.ws_a = reinterpret_cast<float*>(base + w.off_a);
+    a.ws_d = reinterpret_cast<float*>(base + w.off_d);
+    a.ws_bc = reinterpret_cast<float*>(base + w.off_bc);
+    a.nblk = pl.nblk;
+    a.nchains = pl.nchains;
+    a.K = pl.K;
+    a.seg_tiles = pl.seg_tiles;
+    a.ntiles = pl.ntiles;
+    cudaError_t e = cudaMemsetAsync(ws, 0, (size_t)w.off_hand, s);
+    if (e != cudaSuccess) return e;
+    return dtype == 1 ? launch_pb<__half>(a, pl.grid, dA, dB, dC, dD, s)
+                      : launch_pb<float>(a, pl.grid, dA, dB, dC, dD, s);
+}
+
+}  // namespace mwc

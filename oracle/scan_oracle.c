@@ -15,7 +15,9 @@
  *       only reading under which the loop at :920-922 is the recurrence the CUDA kernels
  *       at :93-174 / :611-667 compute.
  *   mamba_windows_cuda/mamba_cuda.py:65-70    safe_exp: the CUDA kernels clamp the exponent
- *       to [-88, 88]; `clamp` != 0 reproduces that (a clamped exponent has zero derivative).
+ *       to [-88, 88]; `clamp` != 0 reproduces that. As in the reference's CUDA backward
+ *       (:724-731), the gradient terms use the clamped factor a with the unclamped
+ *       formulas (d a / d delta taken as A a everywhere).
  *   mamba_windows_cuda/mamba_cuda.py:669-745  the gradients of that recurrence (bwd_direct),
  *       extended with dh_last in and dh_prev out, which the reference's stateful path
  *       (:1044-1096) promises but computes incorrectly.
@@ -135,7 +137,6 @@ ORC_EXPORT void orc_ss_bwd(const double* u, const double* delta, const double* A
         double* myB = pB + (size_t)tid * bln;
         double* myC = pC + (size_t)tid * bln;
         double* hs = (double*)malloc(sizeof(double) * (size_t)((L + 1) * N));
-        double* g = (double*)malloc(sizeof(double) * (size_t)N);
         double* q = (double*)malloc(sizeof(double) * (size_t)N);
         /* d outer so dA[d,:] and dD[d] are owned by exactly one thread */
 #pragma omp for schedule(static)
@@ -171,13 +172,12 @@ ORC_EXPORT void orc_ss_bwd(const double* u, const double* delta, const double* A
                         double gn = gy * Ct[n] + q[n];
                         double hprev = hs[t * N + n];
                         double ah = a * hprev;
+                        (void)inside;
                         dCt[n] += gy * hs[(t + 1) * N + n];
                         dBt[n] += gn * dt * uu;
                         s_gB += gn * Bt[n];
-                        if (inside) {
-                            s_dA += gn * A[d * N + n] * ah;
-                            dA[d * N + n] += gn * dt * ah;
-                        }
+                        s_dA += gn * A[d * N + n] * ah;
+                        dA[d * N + n] += gn * dt * ah;
                         q[n] = a * gn;
                     }
                     du[i] = gy * Dv[d] + dt * s_gB;
@@ -189,7 +189,6 @@ ORC_EXPORT void orc_ss_bwd(const double* u, const double* delta, const double* A
             }
         }
         free(hs);
-        free(g);
         free(q);
     }
     for (size_t k = 0; k < bln; ++k) {

@@ -54,9 +54,12 @@ def test_size_queries(lib):
     assert lib.mwc_ss_ckpt_count(0) == 0
     ws = lib.mwc_ss_bwd_workspace_bytes(4, 2048, 5120, 1)
     assert ws > 4 * 5120 * 17 * 4 and ws % 256 == 0
-    # a long sequence with few channels is scanned in segments and needs carry space
+    # a long sequence with few channels is scanned in parallel segments (carry space);
+    # many channels run the persistent queue (flags + segment hand-off states)
     assert lib.mwc_ss_fwd_workspace_bytes(1, 65536, 2048, 0) > 0
-    assert lib.mwc_ss_fwd_workspace_bytes(4, 2048, 5120, 1) == 0
+    assert lib.mwc_ss_fwd_workspace_bytes(4, 2048, 5120, 1) > 0
+    # few channels and a short sequence: one pass, no workspace
+    assert lib.mwc_ss_fwd_workspace_bytes(1, 256, 128, 0) == 0
 
 
 def test_c_abi_rejects_bad_arguments_without_touching_the_gpu(lib):

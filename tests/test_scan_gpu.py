@@ -330,3 +330,60 @@ def test_parallel_scan_reference_test_shape(mwc):
     A = torch.randn(2, 32, 128, 16, device="cuda").abs() * 0.1
     X = torch.randn(2, 32, 128, 16, device="cuda")
     assert (parallel_scan_fn(A, X) - parallel_scan_ref(A, X)).abs().max().item() < 1e-4
+
+
+# ------------------------------------------------------------- many-chain (persistent) path
+
+@pytest.mark.parametrize("dtype,D,L", [(torch.float32, 5120, 250), (torch.float16, 5120, 256),
+                                       (torch.float32, 5100, 200)])
+def test_persistent_forward_many_chains(mwc, dtype, D, L):
+    """B*D/128 >= #SMs: the forward runs as a persistent TMA kernel over a queue of
+    (128-channel block, L-segment) units with state hand-off between segments."""
+    from mamba_windows_cuda import _lib, _ops
+    B = 4
+    dt = 1 if dtype == torch.float16 else 0
+    assert _lib.load().mwc_ss_fwd_workspace_bytes(B, L, D, dt) > 0
+    x = make_inputs(B, L, D, dtype, seed=31 + D + L, with_state=True, device="cuda")
+    args = [x[k] for k in ("u", "delta", "A", "Bm", "Cm", "Dv")]
+    out, h_last, ckpt, decay = _ops.ss_forward(*args, x["h_prev"], want_h_last=True,
+                                               want_ckpt=True, want_decay=True)
+    ref_out, ref_h = oracle_fwd(x, x["h_prev"])
+    check = (lambda a, r, w: assert_fp32(a, r, what=w)) if dtype == torch.float32 else \
+        (lambda a, r, w: assert_fp16(a, r, w))
+    check(out, ref_out, "out")
+    check(h_last, ref_h, "h_last")
+    k = (L - 1) // 16 // 2
+    _, h_k = O.ss_fwd(*[np64(x[n][:, :16 * (k + 1)] if n in ("u", "delta", "Bm", "Cm") else x[n])
+                        for n in ("u", "delta", "A", "Bm", "Cm", "Dv")], np64(x["h_prev"]))
+    assert_fp32(ckpt[:, k], h_k, tol=1e-4 if dtype == torch.float32 else 1e-2, what="ckpt")
+    ref_decay = torch.exp(x["delta"].double().sum(1).unsqueeze(-1) * x["A"].double().unsqueeze(0))
+    assert_fp32(decay, ref_decay.cpu().numpy(), tol=1e-4 if dtype == torch.float32 else 1e-2,
+                what="decay")
+    assert _lib.load().mwc_ss_bwd_workspace_bytes(B, L, D, dt) > 0
+    _, _, grads = run_stateful(mwc, x, x["h_prev"], x["gh"])
+    ref = oracle_bwd(x, x["h_prev"], x["gh"])
+    for k2 in GRADS + ("dh_prev",):
+        if dtype == torch.float32:
+            assert_fp32(grads[k2], ref[k2], what=k2)
+        else:
+            scale = max(1.0, float(np.abs(ref[k2]).max()))
+            assert_fp16(grads[k2], ref[k2], k2, atol=2e-2 * scale, rtol=1e-2)
+
+
+def test_persistent_backward_is_deterministic(mwc):
+    x = make_inputs(4, 300, 5120, torch.float16, seed=9, with_state=True, device="cuda")
+    _, _, g1 = run_stateful(mwc, x, x["h_prev"], x["gh"])
+    _, _, g2 = run_stateful(mwc, x, x["h_prev"], x["gh"])
+    for k in g1:
+        assert torch.equal(g1[k], g2[k]), k
+
+
+def test_persistent_forward_is_deterministic_and_ckpt_only(mwc):
+    from mamba_windows_cuda import _ops
+    x = make_inputs(4, 512, 5120, torch.float16, seed=2, device="cuda")
+    args = [x[k] for k in ("u", "delta", "A", "Bm", "Cm", "Dv")]
+    o1, h1, c1, _ = _ops.ss_forward(*args, want_h_last=True, want_ckpt=True)
+    o2, h2, c2, _ = _ops.ss_forward(*args, want_h_last=True, want_ckpt=True)
+    _, h3, c3, _ = _ops.ss_forward(*args, want_out=False, want_h_last=True, want_ckpt=True)
+    assert torch.equal(o1, o2) and torch.equal(h1, h2) and torch.equal(c1, c2)
+    assert torch.equal(h1, h3) and torch.equal(c1, c3)
