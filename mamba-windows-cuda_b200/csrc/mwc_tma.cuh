@@ -11,6 +11,7 @@ namespace mwc {
 // Error codes written to the workspace error word.
 constexpr int ERR_WAIT_TMA = 1;     // a TMA tile never arrived
 constexpr int ERR_WAIT_CHAIN = 2;   // the previous segment of a chain never published its state
+constexpr int ERR_SMEM_ALIGN = 3;   // dynamic shared memory not 128-byte aligned (kernel exits)
 constexpr unsigned WAIT_SPINS = 1u << 24;   // a few seconds with the backoff below
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -30,21 +30,25 @@ namespace mwc {
 
 constexpr int PB_LT = CK;     // 16 steps per tile
 constexpr int PB_CPB = 128;
-constexpr int PB_NT = 128;
+constexpr int PB_NT = 256;    // 8 warps: two warps per SM sub-partition
+constexpr int PB_NW = PB_NT / 32;
 constexpr int PB_ST = 2;
+#ifndef MWC_BWD_MIN_SEG_TILES
+#define MWC_BWD_MIN_SEG_TILES 4   // shortest segment (in 16-step tiles) the planner may pick
+#endif
 
 template <typename T>
-struct __align__(1024) PBwdSmem {
-    float4 hc[PB_LT][4][PB_NT];                 // state cache: [step][channel c][thread]
+struct __align__(128) PBwdSmem {
+    float4 hc[PB_LT][2][PB_NT];                 // state cache: [step][channel c][thread]
     float h0[PB_ST][PB_CPB][NSTATE];            // checkpoint at the chunk start
     T u[PB_ST][PB_LT][PB_CPB];
     T d[PB_ST][PB_LT][PB_CPB];
     T g[PB_ST][PB_LT][PB_CPB];
     T Bt[PB_ST][PB_LT][NSTATE];
     T Ct[PB_ST][PB_LT][NSTATE];
-    float red[2][PB_NT / 32][PB_LT][2 * NSTATE];  // per-warp dB | dC partials, double buffered
-    float Bf[sizeof(T) == 2 ? PB_NT / 32 : 1][PB_LT][NSTATE];
-    float Cf[sizeof(T) == 2 ? PB_NT / 32 : 1][PB_LT][NSTATE];
+    float red[PB_NW][PB_LT][2 * NSTATE];        // per-warp dB | dC partials of the tile
+    float Bf[PB_LT][NSTATE];                    // float32 copies of B / C (fp16 inputs)
+    float Cf[PB_LT][NSTATE];
     uint64_t full[PB_ST];
     int unit[PB_ST];
     int tile[PB_ST];
@@ -56,6 +60,19 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, unsigned b
             smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
+}
+
+template <typename T>
+__device__ __forceinline__ void load2(float (&v)[2], const T* p);
+template <>
+__device__ __forceinline__ void load2<float>(float (&v)[2], const float* p) {
+    const float2 x = *reinterpret_cast<const float2*>(p);
+    v[0] = x.x; v[1] = x.y;
+}
+template <>
+__device__ __forceinline__ void load2<__half>(float (&v)[2], const __half* p) {
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(p));
+    v[0] = a.x; v[1] = a.y;
 }
 
 template <typename T>
@@ -71,6 +88,17 @@ __device__ __forceinline__ void load4<__half>(float (&v)[4], const __half* p) {
     const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
     const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
     v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+}
+
+template <typename T>
+__device__ __forceinline__ void store2(T* p, float a, float b);
+template <>
+__device__ __forceinline__ void store2<float>(float* p, float a, float b) {
+    *reinterpret_cast<float2*>(p) = make_float2(a, b);
+}
+template <>
+__device__ __forceinline__ void store2<__half>(__half* p, float a, float b) {
+    *reinterpret_cast<__half2*>(p) = __floats2half2_rn(a, b);
 }
 
 template <typename T>
@@ -95,15 +123,21 @@ __device__ __forceinline__ float2 ex2_clamped(float2 x) {
     return make_float2(ex2(fminf(x.x, ARG2_HI)), ex2(fminf(x.y, ARG2_HI)));
 }
 
+// Thread layout: warp w covers channels 16w .. 16w+15; lane = (cg, sg) with cg = lane / 4
+// the channel pair (2 adjacent channels) and sg = lane % 4 the state group (4 states).
 template <typename T>
 __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __grid_constant__ PBwdArgs p) {
-    extern __shared__ uint8_t smem_raw[];
-    PBwdSmem<T>& s = *reinterpret_cast<PBwdSmem<T>*>(
-        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    // Direct cast (no integer round trip): accesses stay in the shared address space.
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    PBwdSmem<T>& s = *reinterpret_cast<PBwdSmem<T>*>(smem_raw);
+    if ((smem_u32(smem_raw) & 127u) != 0u) {  // TMA destinations need 128-byte alignment
+        if (threadIdx.x == 0) atomicCAS(p.err, 0, ERR_SMEM_ALIGN);
+        return;
+    }
     constexpr bool HALF = sizeof(T) == 2;
     const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
     const int cg = lane >> 2, sg = lane & 3;
-    const int c4 = w * 32 + cg * 4;          // first of the thread's 4 channels in the block
+    const int c2 = w * 16 + cg * 2;          // first of the thread's 2 channels in the block
     const int total = p.nchains * p.K;
     const int64_t Lp = (int64_t)p.nck * CK;
     const unsigned tile_bytes = (unsigned)((3 * PB_LT * PB_CPB + 2 * PB_LT * NSTATE) * sizeof(T));
@@ -162,28 +196,15 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
 
     const T* Ap = static_cast<const T*>(p.A);
     const T* Dp = static_cast<const T*>(p.Dv);
-    float2 A2[4][2], q[4][2], dA[4][2];
-    float Dd[4], dD[4];
-    int64_t dbase = 0;                      // first of the 4 channels (global index)
-    int prev_blk = 0, prev_b = 0, prev_t0 = 0;
+    float2 A2[2][2], q[2][2], dA[2][2];
+    float Dd[2], dD[2];
+    int64_t dbase = 0;                      // first of the 2 channels (global index)
+    const int oidx = (cg < 4) ? (4 * sg + cg) : (NSTATE + 4 * sg + cg - 4);
 
     for (int it = 0;; ++it) {
         const int st = it % PB_ST;
         const unsigned phase = (unsigned)(it / PB_ST) & 1u;
         const int unit = s.unit[st];
-
-        // dB | dC partials of the previous tile: sum the 4 warps in order, one row per step
-        if (it > 0) {
-            const int pb = (it - 1) & 1;
-            float* wb = p.ws_bc + (((int64_t)prev_blk * p.B + prev_b) * Lp + prev_t0) * (2 * NSTATE);
-#pragma unroll
-            for (int r = 0; r < (PB_LT * 2 * NSTATE) / PB_NT; ++r) {
-                const int idx = tid + r * PB_NT;
-                const int i = idx / (2 * NSTATE), v = idx % (2 * NSTATE);
-                wb[idx] = ((s.red[pb][0][i][v] + s.red[pb][1][i][v]) + s.red[pb][2][i][v]) +
-                          s.red[pb][3][i][v];
-            }
-        }
         if (unit < 0) break;
 
         const int pc = s.tile[st];
@@ -194,14 +215,14 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
         const int tix = first + ntl - 1 - pc;
         const int t0 = tix * PB_LT;
         const bool unit_end = pc == ntl - 1;
-        bool dvc[4];
+        bool dvc[2];
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) dvc[cc] = (int64_t)blk * PB_CPB + c4 + cc < p.D;
+        for (int cc = 0; cc < 2; ++cc) dvc[cc] = (int64_t)blk * PB_CPB + c2 + cc < p.D;
 
         if (pc == 0) {  // unit start
-            dbase = (int64_t)blk * PB_CPB + c4;
+            dbase = (int64_t)blk * PB_CPB + c2;
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
+            for (int cc = 0; cc < 2; ++cc) {
                 float a4[4] = {0.f, 0.f, 0.f, 0.f};
                 if (dvc[cc]) load4<T>(a4, Ap + (dbase + cc) * NSTATE + 4 * sg);
                 A2[cc][0] = make_float2(a4[0] * LOG2E, a4[1] * LOG2E);
@@ -212,7 +233,7 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
             }
             if (kp == 0) {
 #pragma unroll
-                for (int cc = 0; cc < 4; ++cc) {
+                for (int cc = 0; cc < 2; ++cc) {
                     float g4[4] = {0.f, 0.f, 0.f, 0.f};
                     if (p.dh_last != nullptr && dvc[cc])
                         load4<T>(g4, static_cast<const T*>(p.dh_last) + ((int64_t)b * p.D + dbase + cc) * NSTATE + 4 * sg);
@@ -222,9 +243,9 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
             } else {
                 if (tid == 0) flag_wait(&p.flags[c * p.K + kp - 1], 1, p.err);
                 __syncthreads();
-                const float* hs = p.hand + ((int64_t)(c * p.K + kp - 1) * PB_CPB + c4) * NSTATE + 4 * sg;
+                const float* hs = p.hand + ((int64_t)(c * p.K + kp - 1) * PB_CPB + c2) * NSTATE + 4 * sg;
 #pragma unroll
-                for (int cc = 0; cc < 4; ++cc) {
+                for (int cc = 0; cc < 2; ++cc) {
                     const float4 v = __ldcg(reinterpret_cast<const float4*>(hs + cc * NSTATE));
                     q[cc][0] = make_float2(v.x, v.y);
                     q[cc][1] = make_float2(v.z, v.w);
@@ -233,28 +254,24 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
         }
 
         mbar_wait(&s.full[st], phase, p.err);
-        const float* Bf;
-        const float* Cf;
         if constexpr (HALF) {
-            for (int idx = lane; idx < PB_LT * NSTATE; idx += 32) {
-                (&s.Bf[w][0][0])[idx] = to_f((&s.Bt[st][0][0])[idx]);
-                (&s.Cf[w][0][0])[idx] = to_f((&s.Ct[st][0][0])[idx]);
+            for (int idx = tid; idx < PB_LT * NSTATE; idx += PB_NT) {
+                (&s.Bf[0][0])[idx] = to_f((&s.Bt[st][0][0])[idx]);
+                (&s.Cf[0][0])[idx] = to_f((&s.Ct[st][0][0])[idx]);
             }
-            __syncwarp();
-            Bf = &s.Bf[w][0][0];
-            Cf = &s.Cf[w][0][0];
-        } else {
-            Bf = reinterpret_cast<const float*>(&s.Bt[st][0][0]);
-            Cf = reinterpret_cast<const float*>(&s.Ct[st][0][0]);
         }
+        // also orders the previous tile's reads of red before this tile's writes
+        __syncthreads();
+        const float* Bf = HALF ? &s.Bf[0][0] : reinterpret_cast<const float*>(&s.Bt[st][0][0]);
+        const float* Cf = HALF ? &s.Cf[0][0] : reinterpret_cast<const float*>(&s.Ct[st][0][0]);
 
         // state at the chunk start
-        float2 h[4][2];
+        float2 h[2][2];
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
+        for (int cc = 0; cc < 2; ++cc) {
             float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
             if (tix > 0) {
-                v = *reinterpret_cast<const float4*>(&s.h0[st][c4 + cc][4 * sg]);
+                v = *reinterpret_cast<const float4*>(&s.h0[st][c2 + cc][4 * sg]);
             } else if (p.h_prev != nullptr && dvc[cc]) {
                 float hp4[4];
                 load4<T>(hp4, static_cast<const T*>(p.h_prev) + ((int64_t)b * p.D + dbase + cc) * NSTATE + 4 * sg);
@@ -263,56 +280,68 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
             h[cc][0] = make_float2(v.x, v.y);
             h[cc][1] = make_float2(v.z, v.w);
         }
-        float2 h0[4][2];
+        float2 h0[2][2];
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
+        for (int cc = 0; cc < 2; ++cc) {
             h0[cc][0] = h[cc][0];
             h0[cc][1] = h[cc][1];
         }
 
-        // ---- recompute the chunk's states -------------------------------------------
-#pragma unroll 2
-        for (int i = 0; i < PB_LT; ++i) {
-            float dt[4], uu[4];
-            load4<T>(dt, &s.d[st][i][c4]);
-            load4<T>(uu, &s.u[st][i][c4]);
-            const float4 B4 = *reinterpret_cast<const float4*>(Bf + i * NSTATE + 4 * sg);
-            const float2 Bp0 = make_float2(B4.x, B4.y), Bp1 = make_float2(B4.z, B4.w);
+        // ---- recompute the chunk's states (blocks of 4 steps: loads, then stores) ----
+#pragma unroll 1
+        for (int i0 = 0; i0 < PB_LT; i0 += 4) {
+            float dt[4][2], uu[4][2];
+            float4 B4[4];
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
-                const float2 dt2 = f2(dt[cc]);
-                const float2 du2 = f2(dt[cc] * uu[cc]);
-                const float2 a0 = ex2_clamped(__fmul2_rn(dt2, A2[cc][0]));
-                const float2 a1 = ex2_clamped(__fmul2_rn(dt2, A2[cc][1]));
-                h[cc][0] = __ffma2_rn(a0, h[cc][0], __fmul2_rn(du2, Bp0));
-                h[cc][1] = __ffma2_rn(a1, h[cc][1], __fmul2_rn(du2, Bp1));
-                s.hc[i][cc][tid] = make_float4(h[cc][0].x, h[cc][0].y, h[cc][1].x, h[cc][1].y);
+            for (int r = 0; r < 4; ++r) {
+                load2<T>(dt[r], &s.d[st][i0 + r][c2]);
+                load2<T>(uu[r], &s.u[st][i0 + r][c2]);
+                B4[r] = *reinterpret_cast<const float4*>(Bf + (i0 + r) * NSTATE + 4 * sg);
+            }
+            float4 hv[4][2];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const float2 Bp0 = make_float2(B4[r].x, B4[r].y), Bp1 = make_float2(B4[r].z, B4[r].w);
+#pragma unroll
+                for (int cc = 0; cc < 2; ++cc) {
+                    const float2 dt2 = f2(dt[r][cc]);
+                    const float2 du2 = f2(dt[r][cc] * uu[r][cc]);
+                    const float2 a0 = ex2_clamped(__fmul2_rn(dt2, A2[cc][0]));
+                    const float2 a1 = ex2_clamped(__fmul2_rn(dt2, A2[cc][1]));
+                    h[cc][0] = __ffma2_rn(a0, h[cc][0], __fmul2_rn(du2, Bp0));
+                    h[cc][1] = __ffma2_rn(a1, h[cc][1], __fmul2_rn(du2, Bp1));
+                    hv[r][cc] = make_float4(h[cc][0].x, h[cc][0].y, h[cc][1].x, h[cc][1].y);
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                s.hc[i0 + r][0][tid] = hv[r][0];
+                s.hc[i0 + r][1][tid] = hv[r][1];
             }
         }
 
         // ---- adjoint pass -------------------------------------------------------------
         T* dub = static_cast<T*>(p.du);
         T* ddb = static_cast<T*>(p.ddelta);
-        float2 ht[4][2];
+        float2 ht[2][2];
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
+        for (int cc = 0; cc < 2; ++cc) {
             ht[cc][0] = h[cc][0];
             ht[cc][1] = h[cc][1];
         }
-        const int oidx = (cg < 4) ? (4 * sg + cg) : (NSTATE + 4 * sg + cg - 4);
 #pragma unroll 1
         for (int i = PB_LT - 1; i >= 0; --i) {
-            float dt[4], uu[4], gy[4];
-            load4<T>(dt, &s.d[st][i][c4]);
-            load4<T>(uu, &s.u[st][i][c4]);
-            load4<T>(gy, &s.g[st][i][c4]);
+            float dt[2], uu[2], gy[2];
+            load2<T>(dt, &s.d[st][i][c2]);
+            load2<T>(uu, &s.u[st][i][c2]);
+            load2<T>(gy, &s.g[st][i][c2]);
             const float4 B4 = *reinterpret_cast<const float4*>(Bf + i * NSTATE + 4 * sg);
             const float4 C4 = *reinterpret_cast<const float4*>(Cf + i * NSTATE + 4 * sg);
             const float2 Bp[2] = {make_float2(B4.x, B4.y), make_float2(B4.z, B4.w)};
             const float2 Cp[2] = {make_float2(C4.x, C4.y), make_float2(C4.z, C4.w)};
-            float2 hp[4][2];
+            float2 hp[2][2];
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
+            for (int cc = 0; cc < 2; ++cc) {
                 if (i > 0) {
                     const float4 v = s.hc[i - 1][cc][tid];
                     hp[cc][0] = make_float2(v.x, v.y);
@@ -324,9 +353,9 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
             }
             float2 vB[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
             float2 vC[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-            float S1[4], S2[4];
+            float S1[2], S2[2];
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
+            for (int cc = 0; cc < 2; ++cc) {
                 const float2 dt2 = f2(dt[cc]);
                 const float2 du2 = f2(dt[cc] * uu[cc]);
                 const float2 gy2 = f2(gy[cc]);
@@ -351,33 +380,12 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
 #pragma unroll
             for (int o = 1; o <= 2; o <<= 1) {
 #pragma unroll
-                for (int cc = 0; cc < 4; ++cc) {
+                for (int cc = 0; cc < 2; ++cc) {
                     S1[cc] += __shfl_xor_sync(FULL, S1[cc], o);
                     S2[cc] += __shfl_xor_sync(FULL, S2[cc], o);
                 }
             }
-            const int t = t0 + i;
-            if (sg == 0 && t < p.L) {
-                float duo[4], ddo[4];
-#pragma unroll
-                for (int cc = 0; cc < 4; ++cc) {
-                    duo[cc] = fmaf(gy[cc], Dd[cc], dt[cc] * S2[cc]);
-                    ddo[cc] = fmaf(uu[cc], S2[cc], S1[cc] * LN2);
-                }
-                const int64_t off = ((int64_t)b * p.L + t) * p.D + dbase;
-                if (dvc[3]) {
-                    store4<T>(dub + off, duo);
-                    store4<T>(ddb + off, ddo);
-                } else {
-#pragma unroll
-                    for (int cc = 0; cc < 4; ++cc)
-                        if (dvc[cc]) {
-                            dub[off + cc] = from_f<T>(duo[cc]);
-                            ddb[off + cc] = from_f<T>(ddo[cc]);
-                        }
-                }
-            }
-            // dB | dC over the warp's 8 channel groups: reduce-scatter (xor 16, 8, 4)
+            // dB | dC over the warp's 8 channel pairs: reduce-scatter (xor 16, 8, 4)
             float v[8] = {vB[0].x, vB[0].y, vB[1].x, vB[1].y, vC[0].x, vC[0].y, vC[1].x, vC[1].y};
 #pragma unroll
             for (int m = 4; m >= 1; m >>= 1) {
@@ -389,42 +397,66 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                     v[j] = keep + __shfl_xor_sync(FULL, send, m * 4);
                 }
             }
-            s.red[it & 1][w][i][oidx] = v[0];
+            s.red[w][i][oidx] = v[0];
+            const int t = t0 + i;
+            if (sg == 0 && t < p.L) {
+                const float du0 = fmaf(gy[0], Dd[0], dt[0] * S2[0]);
+                const float du1 = fmaf(gy[1], Dd[1], dt[1] * S2[1]);
+                const float dd0 = fmaf(uu[0], S2[0], S1[0] * LN2);
+                const float dd1 = fmaf(uu[1], S2[1], S1[1] * LN2);
+                const int64_t off = ((int64_t)b * p.L + t) * p.D + dbase;
+                if (dvc[1]) {
+                    store2<T>(dub + off, du0, du1);
+                    store2<T>(ddb + off, dd0, dd1);
+                } else if (dvc[0]) {
+                    dub[off] = from_f<T>(du0);
+                    ddb[off] = from_f<T>(dd0);
+                }
+            }
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
+            for (int cc = 0; cc < 2; ++cc) {
                 ht[cc][0] = hp[cc][0];
                 ht[cc][1] = hp[cc][1];
             }
         }
 
         if (unit_end) {
-            const int64_t ub = (int64_t)unit * PB_CPB + c4;
+            const int64_t ub = (int64_t)unit * PB_CPB + c2;
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc)
+            for (int cc = 0; cc < 2; ++cc)
                 *reinterpret_cast<float4*>(p.ws_a + (ub + cc) * NSTATE + 4 * sg) =
                     make_float4(dA[cc][0].x, dA[cc][0].y, dA[cc][1].x, dA[cc][1].y);
-            if (sg == 0)
-                *reinterpret_cast<float4*>(p.ws_d + ub) = make_float4(dD[0], dD[1], dD[2], dD[3]);
+            if (sg == 0) *reinterpret_cast<float2*>(p.ws_d + ub) = make_float2(dD[0], dD[1]);
             if (k > 0) {
-                float* hs = p.hand + ((int64_t)(c * p.K + kp) * PB_CPB + c4) * NSTATE + 4 * sg;
+                float* hs = p.hand + ((int64_t)(c * p.K + kp) * PB_CPB + c2) * NSTATE + 4 * sg;
 #pragma unroll
-                for (int cc = 0; cc < 4; ++cc)
+                for (int cc = 0; cc < 2; ++cc)
                     *reinterpret_cast<float4*>(hs + cc * NSTATE) =
                         make_float4(q[cc][0].x, q[cc][0].y, q[cc][1].x, q[cc][1].y);
                 __threadfence();
             } else if (p.dh_prev != nullptr) {
 #pragma unroll
-                for (int cc = 0; cc < 4; ++cc)
+                for (int cc = 0; cc < 2; ++cc)
                     if (dvc[cc]) {
                         const float v4[4] = {q[cc][0].x, q[cc][0].y, q[cc][1].x, q[cc][1].y};
                         store4<T>(static_cast<T*>(p.dh_prev) + ((int64_t)b * p.D + dbase + cc) * NSTATE + 4 * sg, v4);
                     }
             }
         }
-        prev_blk = blk;
-        prev_b = b;
-        prev_t0 = t0;
         __syncthreads();
+        // dB | dC partials of this tile: the 8 warps summed in order, one row per step
+        {
+            float* wb = p.ws_bc + (((int64_t)blk * p.B + b) * Lp + t0) * (2 * NSTATE);
+#pragma unroll
+            for (int r = 0; r < (PB_LT * 2 * NSTATE) / PB_NT; ++r) {
+                const int idx = tid + r * PB_NT;
+                const int i = idx / (2 * NSTATE), vv = idx % (2 * NSTATE);
+                float acc = s.red[0][i][vv];
+#pragma unroll
+                for (int ww = 1; ww < PB_NW; ++ww) acc += s.red[ww][i][vv];
+                wb[idx] = acc;
+            }
+        }
         if (tid == 0) {
             if (unit_end && k > 0) flag_release(&p.flags[c * p.K + kp], 1);
             issue(st);
@@ -485,7 +517,7 @@ PersistPlan plan_persistent_bwd(int64_t B, int64_t L, int64_t D, int num_sms) {
     for (int K = 1; K <= pl.ntiles; ++K) {
         const int seg = (pl.ntiles + K - 1) / K;
         if ((pl.ntiles + seg - 1) / seg != K) continue;
-        if (K > 1 && seg < 4) break;
+        if (K > 1 && seg < MWC_BWD_MIN_SEG_TILES) break;
         const int64_t U = (int64_t)pl.nchains * K;
         const int64_t G = std::min<int64_t>(num_sms, U);
         const int64_t waves = (U + G - 1) / G;
@@ -518,7 +550,7 @@ BwdPersistWs bwd_persistent_ws(const PersistPlan& pl, int64_t B, int64_t L) {
 template <typename T>
 static cudaError_t launch_pb(const PBwdArgs& a, int grid, void* dA, void* dB, void* dC, void* dD,
                              cudaStream_t s) {
-    const size_t smem = sizeof(PBwdSmem<T>) + 1024;
+    const size_t smem = sizeof(PBwdSmem<T>);
     cudaError_t e = cudaFuncSetAttribute(ss_bwd_persistent_kernel<T>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;

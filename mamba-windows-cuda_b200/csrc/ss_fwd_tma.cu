@@ -24,30 +24,44 @@ namespace mwc {
 
 constexpr int PF_LT = 32;
 constexpr int PF_CPB = 128;
-constexpr int PF_NT = 128;
+constexpr int PF_NT = 256;   // 8 warps: two warps per SM sub-partition
 constexpr int PF_ST = 3;
+#ifndef MWC_FWD_MIN_SEG_TILES
+#define MWC_FWD_MIN_SEG_TILES 2   // shortest segment (in 32-step tiles) the planner may pick
+#endif
 
 template <typename T>
-struct __align__(1024) PFwdSmem {
+struct __align__(128) PFwdSmem {
     T u[PF_ST][PF_LT][PF_CPB];
     T d[PF_ST][PF_LT][PF_CPB];
     T Bt[PF_ST][PF_LT][NSTATE];
     T Ct[PF_ST][PF_LT][NSTATE];
-    T y[2][PF_LT][PF_CPB];
-    float Bf[PF_NT / 32][PF_LT][NSTATE];   // per-warp float32 copies (fp16 inputs only)
-    float Cf[PF_NT / 32][PF_LT][NSTATE];
+    T y[2][PF_LT][PF_CPB];                 // TMA store staging, double buffered
+    float py[2][PF_LT][PF_CPB];            // partial <C, h> of the two state halves
+    float Bf[PF_LT][NSTATE];               // float32 copies of B / C (fp16 inputs)
+    float Cf[PF_LT][NSTATE];
+    float Ds[PF_CPB];                      // D of the current unit's channels
     uint64_t full[PF_ST];
     int unit[PF_ST];
     int tile[PF_ST];
 };
 
+// Thread layout: tid = half * 128 + channel; half 0 holds states 0-7 of its channel,
+// half 1 states 8-15 (4 float2 pairs each, packed FFMA2). Warps w and w + 4 share the
+// same 32 channels, so every SM sub-partition runs two warps.
 template <typename T>
 __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __grid_constant__ PFwdArgs p) {
-    extern __shared__ uint8_t smem_raw[];
-    PFwdSmem<T>& s = *reinterpret_cast<PFwdSmem<T>*>(
-        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    // Direct cast (no integer round trip): accesses stay in the shared address space.
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    PFwdSmem<T>& s = *reinterpret_cast<PFwdSmem<T>*>(smem_raw);
+    if ((smem_u32(smem_raw) & 127u) != 0u) {  // TMA destinations need 128-byte alignment
+        if (threadIdx.x == 0) atomicCAS(p.err, 0, ERR_SMEM_ALIGN);
+        return;
+    }
     const int tid = threadIdx.x;
-    const int ch = tid;
+    const int ch = tid & (PF_CPB - 1);
+    const int half = tid >> 7;
+    const int n0 = half * 8;               // first state of this thread
     const int total = p.nchains * p.K;
     constexpr bool HALF = sizeof(T) == 2;
     const unsigned stage_bytes =
@@ -95,8 +109,8 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
 
     const T* Ap = static_cast<const T*>(p.A);
     const T* Dp = static_cast<const T*>(p.Dv);
-    float2 A2v[8], h2[8];
-    float Dd = 0.f, sumd = 0.f;
+    float2 A2v[4], h2[4];
+    float sumd = 0.f;
     int64_t d = 0;
     bool dv = false;
 
@@ -115,26 +129,27 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
             d = (int64_t)blk * PF_CPB + ch;
             dv = d < p.D;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                A2v[j].x = dv ? to_f(Ap[d * NSTATE + 2 * j]) * LOG2E : 0.f;
-                A2v[j].y = dv ? to_f(Ap[d * NSTATE + 2 * j + 1]) * LOG2E : 0.f;
+            for (int j = 0; j < 4; ++j) {
+                A2v[j].x = dv ? to_f(Ap[d * NSTATE + n0 + 2 * j]) * LOG2E : 0.f;
+                A2v[j].y = dv ? to_f(Ap[d * NSTATE + n0 + 2 * j + 1]) * LOG2E : 0.f;
             }
-            Dd = dv ? to_f(Dp[d]) : 0.f;
+            if (half == 0) s.Ds[ch] = dv ? to_f(Dp[d]) : 0.f;
             if (k == 0) {
                 sumd = 0.f;
 #pragma unroll
-                for (int j = 0; j < 8; ++j) h2[j] = make_float2(0.f, 0.f);
+                for (int j = 0; j < 4; ++j) h2[j] = make_float2(0.f, 0.f);
                 if (p.h_prev != nullptr && dv) {
-                    const T* hp = static_cast<const T*>(p.h_prev) + ((int64_t)b * p.D + d) * NSTATE;
+                    const T* hp = static_cast<const T*>(p.h_prev) + ((int64_t)b * p.D + d) * NSTATE + n0;
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) h2[j] = make_float2(to_f(hp[2 * j]), to_f(hp[2 * j + 1]));
+                    for (int j = 0; j < 4; ++j) h2[j] = make_float2(to_f(hp[2 * j]), to_f(hp[2 * j + 1]));
                 }
             } else {
                 if (tid == 0) flag_wait(&p.flags[c * p.K + k - 1], 1, p.err);
                 __syncthreads();
                 const float* hs = p.hand + ((int64_t)(c * p.K + k - 1) * PF_CPB + ch) * (NSTATE + 1);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) h2[j] = make_float2(__ldcg(hs + 2 * j), __ldcg(hs + 2 * j + 1));
+                for (int j = 0; j < 4; ++j)
+                    h2[j] = make_float2(__ldcg(hs + n0 + 2 * j), __ldcg(hs + n0 + 2 * j + 1));
                 sumd = __ldcg(hs + NSTATE);
             }
         }
@@ -143,58 +158,66 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
         const float* Bf;
         const float* Cf;
         if constexpr (HALF) {
-            // each warp converts its own float32 copy of the B / C rows: no CTA barrier
-            const int w = tid >> 5, ln = tid & 31;
-            for (int idx = ln; idx < PF_LT * NSTATE; idx += 32) {
-                (&s.Bf[w][0][0])[idx] = to_f((&s.Bt[st][0][0])[idx]);
-                if (p.has_out) (&s.Cf[w][0][0])[idx] = to_f((&s.Ct[st][0][0])[idx]);
+            for (int idx = tid; idx < PF_LT * NSTATE; idx += PF_NT) {
+                (&s.Bf[0][0])[idx] = to_f((&s.Bt[st][0][0])[idx]);
+                if (p.has_out) (&s.Cf[0][0])[idx] = to_f((&s.Ct[st][0][0])[idx]);
             }
-            __syncwarp();
-            Bf = &s.Bf[w][0][0];
-            Cf = &s.Cf[w][0][0];
+            __syncthreads();
+            Bf = &s.Bf[0][0];
+            Cf = &s.Cf[0][0];
         } else {
             Bf = reinterpret_cast<const float*>(&s.Bt[st][0][0]);
             Cf = reinterpret_cast<const float*>(&s.Ct[st][0][0]);
         }
-        T (*yb)[PF_CPB] = s.y[it & 1];
 
-        // Branch-free step: the exponent clamp of safe_exp is a min per state, so the
-        // unrolled steps can interleave (exponentials of step i+1 overlap the FMAs of i).
-#pragma unroll 4
-        for (int i = 0; i < PF_LT; ++i) {
-            const float dt = to_f(s.d[st][i][ch]);
-            const float uu = to_f(s.u[st][i][ch]);
-            sumd += dt;
-            const float du = dt * uu;
-            const float2 dt2 = make_float2(dt, dt), du2 = make_float2(du, du);
-            float2 a2[8];
+        // Blocks of 8 steps: the block's shared-memory reads precede its stores, and the
+        // exponent clamp of safe_exp is a branch-free min per state, so the exponentials
+        // of later steps overlap the FMAs of earlier ones.
+#pragma unroll 1
+        for (int i0 = 0; i0 < PF_LT; i0 += 8) {
+            float dtv[8], uv[8], yv[8];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const float2 x = __fmul2_rn(dt2, A2v[j]);
-                a2[j] = make_float2(ex2(fminf(x.x, ARG2_HI)), ex2(fminf(x.y, ARG2_HI)));
+            for (int r = 0; r < 8; ++r) {
+                dtv[r] = to_f(s.d[st][i0 + r][ch]);
+                uv[r] = to_f(s.u[st][i0 + r][ch]);
             }
-            const float4* Bq = reinterpret_cast<const float4*>(Bf + i * NSTATE);
-            const float4* Cq = reinterpret_cast<const float4*>(Cf + i * NSTATE);
-            float2 yq[4];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const float4 bq = Bq[q];
-                const float4 cq = Cq[q];
-                h2[2 * q] = __ffma2_rn(a2[2 * q], h2[2 * q], __fmul2_rn(du2, make_float2(bq.x, bq.y)));
-                h2[2 * q + 1] =
-                    __ffma2_rn(a2[2 * q + 1], h2[2 * q + 1], __fmul2_rn(du2, make_float2(bq.z, bq.w)));
-                yq[q] = __fmul2_rn(make_float2(cq.x, cq.y), h2[2 * q]);
-                yq[q] = __ffma2_rn(make_float2(cq.z, cq.w), h2[2 * q + 1], yq[q]);
+            for (int r = 0; r < 8; ++r) {
+                const float dt = dtv[r];
+                sumd += dt;
+                const float2 dt2 = make_float2(dt, dt);
+                const float2 du2 = make_float2(dt * uv[r], dt * uv[r]);
+                float2 a2[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float2 x = __fmul2_rn(dt2, A2v[j]);
+                    a2[j] = make_float2(ex2(fminf(x.x, ARG2_HI)), ex2(fminf(x.y, ARG2_HI)));
+                }
+                const float4* Bq = reinterpret_cast<const float4*>(Bf + (i0 + r) * NSTATE + n0);
+                const float4* Cq = reinterpret_cast<const float4*>(Cf + (i0 + r) * NSTATE + n0);
+                float2 yq[2];
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    const float4 bq = Bq[q];
+                    const float4 cq = Cq[q];
+                    h2[2 * q] = __ffma2_rn(a2[2 * q], h2[2 * q], __fmul2_rn(du2, make_float2(bq.x, bq.y)));
+                    h2[2 * q + 1] =
+                        __ffma2_rn(a2[2 * q + 1], h2[2 * q + 1], __fmul2_rn(du2, make_float2(bq.z, bq.w)));
+                    yq[q] = __fmul2_rn(make_float2(cq.x, cq.y), h2[2 * q]);
+                    yq[q] = __ffma2_rn(make_float2(cq.z, cq.w), h2[2 * q + 1], yq[q]);
+                }
+                const float2 y2 = __fadd2_rn(yq[0], yq[1]);
+                yv[r] = y2.x + y2.y;
             }
-            const float2 y2 = __fadd2_rn(__fadd2_rn(yq[0], yq[1]), __fadd2_rn(yq[2], yq[3]));
-            yb[i][ch] = from_f<T>(fmaf(Dd, uu, y2.x + y2.y));
-            if ((i + 1) % CK == 0 && p.ckpt != nullptr) {
-                const int64_t kk = (int64_t)(t0 + i + 1) / CK - 1;
+#pragma unroll
+            for (int r = 0; r < 8; ++r) s.py[half][i0 + r][ch] = yv[r];
+            if ((i0 + 8) % CK == 0 && p.ckpt != nullptr) {
+                const int64_t kk = (int64_t)(t0 + i0 + 8) / CK - 1;
                 if (kk < p.nck && dv) {
-                    float4* cp = reinterpret_cast<float4*>(p.ckpt + (((int64_t)b * p.nck + kk) * p.D + d) * NSTATE);
-#pragma unroll
-                    for (int q = 0; q < 4; ++q)
-                        cp[q] = make_float4(h2[2 * q].x, h2[2 * q].y, h2[2 * q + 1].x, h2[2 * q + 1].y);
+                    float4* cp = reinterpret_cast<float4*>(
+                        p.ckpt + (((int64_t)b * p.nck + kk) * p.D + d) * NSTATE + n0);
+                    cp[0] = make_float4(h2[0].x, h2[0].y, h2[1].x, h2[1].y);
+                    cp[1] = make_float4(h2[2].x, h2[2].y, h2[3].x, h2[3].y);
                 }
             }
         }
@@ -203,25 +226,25 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
             if (k < p.K - 1) {
                 float* hs = p.hand + ((int64_t)(c * p.K + k) * PF_CPB + ch) * (NSTATE + 1);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    hs[2 * j] = h2[j].x;
-                    hs[2 * j + 1] = h2[j].y;
+                for (int j = 0; j < 4; ++j) {
+                    hs[n0 + 2 * j] = h2[j].x;
+                    hs[n0 + 2 * j + 1] = h2[j].y;
                 }
-                hs[NSTATE] = sumd;
+                if (half == 0) hs[NSTATE] = sumd;
                 __threadfence();
             } else if (dv) {
                 if (p.h_last != nullptr) {
-                    T* hl = static_cast<T*>(p.h_last) + ((int64_t)b * p.D + d) * NSTATE;
+                    T* hl = static_cast<T*>(p.h_last) + ((int64_t)b * p.D + d) * NSTATE + n0;
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
+                    for (int j = 0; j < 4; ++j) {
                         hl[2 * j] = from_f<T>(h2[j].x);
                         hl[2 * j + 1] = from_f<T>(h2[j].y);
                     }
                 }
                 if (p.decay != nullptr) {
-                    float* dc = p.decay + ((int64_t)b * p.D + d) * NSTATE;
+                    float* dc = p.decay + ((int64_t)b * p.D + d) * NSTATE + n0;
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
+                    for (int j = 0; j < 4; ++j) {
                         dc[2 * j] = ex2(fminf(A2v[j].x * sumd, ARG2_HI));
                         dc[2 * j + 1] = ex2(fminf(A2v[j].y * sumd, ARG2_HI));
                     }
@@ -229,13 +252,30 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
             }
         }
 
-        // End of tile: the y buffer of tile it-1 must be drained before tile it+1 writes it.
-        if (tid == 0) bulk_wait_read0();
+        // y = partial(states 0-7) + partial(states 8-15) + D u, staged for the TMA store.
+        // The staging buffer of this tile was last read by the store of tile it-2.
+        if (tid == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+        __syncthreads();
+        if (p.has_out) {
+            T (*yb)[PF_CPB] = s.y[it & 1];
+#pragma unroll
+            for (int r = 0; r < (PF_LT * PF_CPB) / (4 * PF_NT); ++r) {
+                const int idx = (tid + r * PF_NT) * 4;
+                const int i = idx / PF_CPB, cc = idx % PF_CPB;
+                const float4 p0 = *reinterpret_cast<const float4*>(&s.py[0][i][cc]);
+                const float4 p1 = *reinterpret_cast<const float4*>(&s.py[1][i][cc]);
+                const float4 dd = *reinterpret_cast<const float4*>(&s.Ds[cc]);
+                yb[i][cc + 0] = from_f<T>(fmaf(dd.x, to_f(s.u[st][i][cc + 0]), p0.x + p1.x));
+                yb[i][cc + 1] = from_f<T>(fmaf(dd.y, to_f(s.u[st][i][cc + 1]), p0.y + p1.y));
+                yb[i][cc + 2] = from_f<T>(fmaf(dd.z, to_f(s.u[st][i][cc + 2]), p0.z + p1.z));
+                yb[i][cc + 3] = from_f<T>(fmaf(dd.w, to_f(s.u[st][i][cc + 3]), p0.w + p1.w));
+            }
+        }
         fence_proxy_async();
         __syncthreads();
         if (tid == 0) {
             if (p.has_out) {
-                tma_store_3d(&p.tm_y, &yb[0][0], blk * PF_CPB, t0, b);
+                tma_store_3d(&p.tm_y, &s.y[it & 1][0][0], blk * PF_CPB, t0, b);
                 bulk_commit();
             }
             if (last && k < p.K - 1) flag_release(&p.flags[c * p.K + k], 1);
@@ -289,7 +329,7 @@ PersistPlan plan_persistent(int64_t B, int64_t L, int64_t D, int num_sms) {
         const int seg = (pl.ntiles + K - 1) / K;
         const int keff = (pl.ntiles + seg - 1) / seg;
         if (keff != K) continue;
-        if (K > 1 && seg < 2) break;
+        if (K > 1 && seg < MWC_FWD_MIN_SEG_TILES) break;
         const int64_t U = (int64_t)pl.nchains * K;
         const int64_t G = std::min<int64_t>(num_sms, U);
         const int64_t waves = (U + G - 1) / G;
@@ -318,7 +358,7 @@ int64_t persistent_ws_header(const PersistPlan& pl) {
 
 template <typename T>
 static cudaError_t launch_pf(const PFwdArgs& a, int grid, cudaStream_t s) {
-    const size_t smem = sizeof(PFwdSmem<T>) + 1024;
+    const size_t smem = sizeof(PFwdSmem<T>);
     cudaError_t e = cudaFuncSetAttribute(ss_fwd_persistent_kernel<T>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
