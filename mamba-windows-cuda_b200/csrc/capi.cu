@@ -134,7 +134,8 @@ int mwc_ss_fwd(const void* u, const void* delta, const void* A, const void* Bm, 
     const size_t es0 = elem_size(dtype);
     const PersistPlan pp = plan_persistent(B, L, D, sms);
     const bool tma_ok = pp.ok && ((D * (int64_t)es0) % 16 == 0) && aligned16(u) &&
-                        aligned16(delta) && aligned16(Bm) && aligned16(Cm) &&
+                        aligned16(delta) && aligned16(Bm) && aligned16(Cm) && aligned16(A) &&
+                        aligned16(Dv) && (!h_prev || aligned16(h_prev)) &&
                         (!out || aligned16(out)) && L <= 0x7fffffffLL && D <= 0x7fffffffLL;
     if (tma_ok) {
         const int64_t pneed = align_up(persistent_ws_bytes(pp), 256);

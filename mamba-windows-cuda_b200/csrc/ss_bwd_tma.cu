@@ -119,10 +119,6 @@ __device__ __forceinline__ void store4<__half>(__half* p, const float (&v)[4]) {
 
 __device__ __forceinline__ float2 f2(float x) { return make_float2(x, x); }
 
-__device__ __forceinline__ float2 ex2_clamped(float2 x) {
-    return make_float2(ex2(fminf(x.x, ARG2_HI)), ex2(fminf(x.y, ARG2_HI)));
-}
-
 // Thread layout: warp w covers channels 16w .. 16w+15; lane = (cg, sg) with cg = lane / 4
 // the channel pair (2 adjacent channels) and sg = lane % 4 the state group (4 states).
 template <typename T>
@@ -198,6 +194,7 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
     const T* Dp = static_cast<const T*>(p.Dv);
     float2 A2[2][2], q[2][2], dA[2][2];
     float Dd[2], dD[2];
+    bool a_nonpos = true;   // warp-uniform: A <= 0, so delta >= 0 keeps every exponent <= 0
     int64_t dbase = 0;                      // first of the 2 channels (global index)
     const int oidx = (cg < 4) ? (4 * sg + cg) : (NSTATE + 4 * sg + cg - 4);
 
@@ -231,6 +228,9 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                 dD[cc] = 0.f;
                 dA[cc][0] = dA[cc][1] = make_float2(0.f, 0.f);
             }
+            a_nonpos = __all_sync(FULL, A2[0][0].x <= 0.f && A2[0][0].y <= 0.f && A2[0][1].x <= 0.f &&
+                                            A2[0][1].y <= 0.f && A2[1][0].x <= 0.f && A2[1][0].y <= 0.f &&
+                                            A2[1][1].x <= 0.f && A2[1][1].y <= 0.f);
             if (kp == 0) {
 #pragma unroll
                 for (int cc = 0; cc < 2; ++cc) {
@@ -299,15 +299,37 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                 B4[r] = *reinterpret_cast<const float4*>(Bf + (i0 + r) * NSTATE + 4 * sg);
             }
             float4 hv[4][2];
+            float dmin = INFINITY;
+#pragma unroll
+            for (int r = 0; r < 4; ++r) dmin = fminf(dmin, fminf(dt[r][0], dt[r][1]));
+            // safe_exp's clamp is the identity when every exponent is <= 0
+            const bool fast = a_nonpos && __all_sync(FULL, dmin >= 0.f);
+            float2 x[4][2][2];
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+#pragma unroll
+                for (int cc = 0; cc < 2; ++cc) {
+                    x[r][cc][0] = __fmul2_rn(f2(dt[r][cc]), A2[cc][0]);
+                    x[r][cc][1] = __fmul2_rn(f2(dt[r][cc]), A2[cc][1]);
+                }
+            if (!fast) {
+#pragma unroll
+                for (int r = 0; r < 4; ++r)
+#pragma unroll
+                    for (int cc = 0; cc < 2; ++cc)
+#pragma unroll
+                        for (int pr = 0; pr < 2; ++pr)
+                            x[r][cc][pr] = make_float2(fminf(x[r][cc][pr].x, ARG2_HI),
+                                                       fminf(x[r][cc][pr].y, ARG2_HI));
+            }
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
                 const float2 Bp0 = make_float2(B4[r].x, B4[r].y), Bp1 = make_float2(B4[r].z, B4[r].w);
 #pragma unroll
                 for (int cc = 0; cc < 2; ++cc) {
-                    const float2 dt2 = f2(dt[r][cc]);
                     const float2 du2 = f2(dt[r][cc] * uu[r][cc]);
-                    const float2 a0 = ex2_clamped(__fmul2_rn(dt2, A2[cc][0]));
-                    const float2 a1 = ex2_clamped(__fmul2_rn(dt2, A2[cc][1]));
+                    const float2 a0 = make_float2(ex2(x[r][cc][0].x), ex2(x[r][cc][0].y));
+                    const float2 a1 = make_float2(ex2(x[r][cc][1].x), ex2(x[r][cc][1].y));
                     h[cc][0] = __ffma2_rn(a0, h[cc][0], __fmul2_rn(du2, Bp0));
                     h[cc][1] = __ffma2_rn(a1, h[cc][1], __fmul2_rn(du2, Bp1));
                     hv[r][cc] = make_float4(h[cc][0].x, h[cc][0].y, h[cc][1].x, h[cc][1].y);
@@ -354,6 +376,19 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
             float2 vB[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
             float2 vC[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
             float S1[2], S2[2];
+            float2 x[2][2];
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) {
+                x[cc][0] = __fmul2_rn(f2(dt[cc]), A2[cc][0]);
+                x[cc][1] = __fmul2_rn(f2(dt[cc]), A2[cc][1]);
+            }
+            if (!(a_nonpos && __all_sync(FULL, dt[0] >= 0.f && dt[1] >= 0.f))) {
+#pragma unroll
+                for (int cc = 0; cc < 2; ++cc)
+#pragma unroll
+                    for (int pr = 0; pr < 2; ++pr)
+                        x[cc][pr] = make_float2(fminf(x[cc][pr].x, ARG2_HI), fminf(x[cc][pr].y, ARG2_HI));
+            }
 #pragma unroll
             for (int cc = 0; cc < 2; ++cc) {
                 const float2 dt2 = f2(dt[cc]);
@@ -362,7 +397,7 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                 float2 s1 = make_float2(0.f, 0.f), s2 = make_float2(0.f, 0.f);
 #pragma unroll
                 for (int pr = 0; pr < 2; ++pr) {
-                    const float2 a = ex2_clamped(__fmul2_rn(dt2, A2[cc][pr]));
+                    const float2 a = make_float2(ex2(x[cc][pr].x), ex2(x[cc][pr].y));
                     const float2 g = __ffma2_rn(gy2, Cp[pr], q[cc][pr]);
                     const float2 pp = __fmul2_rn(g, __fmul2_rn(a, hp[cc][pr]));
                     s1 = __ffma2_rn(A2[cc][pr], pp, s1);

@@ -1,17 +1,24 @@
-// Persistent, TMA-pipelined forward selective scan for sm_100a.
+// Persistent, warp-specialized, TMA-pipelined forward selective scan for sm_100a.
 //
 // Work decomposition: a "chain" is one batch row x 128 channels over all of L; each chain
 // is cut into K time segments. Units (segment k of chain c) are taken from a global
 // atomic counter in segment-major order by one persistent CTA per SM, so the B*D/128
 // chains spread evenly over the SMs even when there are only slightly more chains than SMs
 // (config 3: 160 chains on 148 SMs). Segment k starts from the state segment k-1
-// published (release/acquire flag); because segments are taken in order, the publisher
-// is always a CTA that is already running, so the wait always ends (and is bounded).
+// published (8 per-warp release increments of a flag); because segments are taken in
+// order, the publisher is always a CTA that is already running, so every wait ends (and
+// each wait is bounded).
 //
-// Per CTA: 4 warps, thread = channel, its 16 states in registers (8 float2 pairs updated
-// with packed FFMA2). Tiles of 32 steps of u / delta (32 x 128) and of B / C (32 x 16)
-// arrive by TMA (cp.async.bulk.tensor) into a 3-stage mbarrier ring that runs ahead
-// across unit boundaries; y leaves through a double-buffered TMA store.
+// CTA = 10 warps, no CTA-wide barrier after set-up; mbarriers connect the roles:
+//   * warps 0-7 (compute): thread = (channel, half): 8 of the channel's 16 states in
+//     registers as 4 float2 pairs (packed FFMA2), the two halves' <C, h> meet through one
+//     shuffle; ex2 with log2(e) folded into A; y to a staging tile, float32 checkpoints
+//     every 16 steps straight to global memory;
+//   * warp 8 (producer): unit queue, hand-off waits, TMA loads of u / delta (32 x 128),
+//     B / C (32 x 16) and the segment's incoming state (1-D bulk copy) into a ring of
+//     stages (full / empty mbarriers);
+//   * warp 9 (helper): float32 copies of B / C for fp16 inputs, and the TMA stores of y
+//     from the double-buffered staging tile.
 #include "mwc_device.cuh"
 #include "mwc_internal.h"
 #include "mwc_tma.cuh"
@@ -24,99 +31,237 @@ namespace mwc {
 
 constexpr int PF_LT = 32;
 constexpr int PF_CPB = 128;
-constexpr int PF_NT = 256;   // 8 warps: two warps per SM sub-partition
-constexpr int PF_ST = 3;
+constexpr int PF_NCW = 8;                    // compute warps
+constexpr int PF_NT = (PF_NCW + 2) * 32;     // + producer warp + helper warp
+constexpr int PF_HAND = PF_CPB * (NSTATE + 1);  // floats of one segment hand-off record
 #ifndef MWC_FWD_MIN_SEG_TILES
 #define MWC_FWD_MIN_SEG_TILES 2   // shortest segment (in 32-step tiles) the planner may pick
 #endif
 
 template <typename T>
-struct __align__(128) PFwdSmem {
-    T u[PF_ST][PF_LT][PF_CPB];
-    T d[PF_ST][PF_LT][PF_CPB];
-    T Bt[PF_ST][PF_LT][NSTATE];
-    T Ct[PF_ST][PF_LT][NSTATE];
-    T y[2][PF_LT][PF_CPB];                 // TMA store staging, double buffered
-    float py[2][PF_LT][PF_CPB];            // partial <C, h> of the two state halves
-    float Bf[PF_LT][NSTATE];               // float32 copies of B / C (fp16 inputs)
-    float Cf[PF_LT][NSTATE];
-    float Ds[PF_CPB];                      // D of the current unit's channels
-    uint64_t full[PF_ST];
-    int unit[PF_ST];
-    int tile[PF_ST];
+struct PfCfg {
+    static constexpr int ST = sizeof(T) == 2 ? 4 : 3;   // pipeline depth (stages)
 };
 
-// Thread layout: tid = half * 128 + channel; half 0 holds states 0-7 of its channel,
-// half 1 states 8-15 (4 float2 pairs each, packed FFMA2). Warps w and w + 4 share the
-// same 32 channels, so every SM sub-partition runs two warps.
+template <typename T>
+struct __align__(128) PFwdSmem {
+    static constexpr int ST = PfCfg<T>::ST;
+    T u[ST][PF_LT][PF_CPB];
+    T d[ST][PF_LT][PF_CPB];
+    T Bt[ST][PF_LT][NSTATE];
+    T Ct[ST][PF_LT][NSTATE];
+    T y[2][PF_LT][PF_CPB];                                       // y staging for TMA stores
+    float hin[ST][PF_HAND];                                      // incoming segment state
+    T At[ST][PF_CPB][NSTATE];                                    // unit parameters: A rows,
+    T Ht[ST][PF_CPB][NSTATE];                                    // h_prev rows,
+    T Dt[ST][PF_CPB];                                            // D
+    float Bf[sizeof(T) == 2 ? ST : 1][PF_LT][NSTATE];            // float32 B / C (fp16 only)
+    float Cf[sizeof(T) == 2 ? ST : 1][PF_LT][NSTATE];
+    uint64_t full[ST], conv[ST], empty[ST], yfull[2], yempty[2];
+    int unit[ST];
+    int tile[ST];
+};
+
+// One block of 8 steps for the lane's 8 states (4 float2 pairs). CLAMP applies the
+// safe_exp upper clamp per state; the caller takes the unclamped variant only when every
+// exponent of the block is provably <= 0 (A <= 0 and delta >= 0), where the clamp is the
+// identity.
+template <bool CLAMP>
+__device__ __forceinline__ void fwd_block8(float2 (&h2)[4], const float2 (&A2v)[4],
+                                           const float (&dtv)[8], const float (&uv)[8],
+                                           const float* Bf, const float* Cf, int n0,
+                                           float (&yv)[8]) {
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+        const float2 dt2 = make_float2(dtv[r], dtv[r]);
+        const float du = dtv[r] * uv[r];
+        const float2 du2 = make_float2(du, du);
+        float2 a2[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 x = __fmul2_rn(dt2, A2v[j]);
+            a2[j] = CLAMP ? make_float2(ex2(fminf(x.x, ARG2_HI)), ex2(fminf(x.y, ARG2_HI)))
+                          : make_float2(ex2(x.x), ex2(x.y));
+        }
+        const float4* Bq = reinterpret_cast<const float4*>(Bf + r * NSTATE + n0);
+        const float4* Cq = reinterpret_cast<const float4*>(Cf + r * NSTATE + n0);
+        float2 yq[2];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            const float4 bq = Bq[q];
+            const float4 cq = Cq[q];
+            h2[2 * q] = __ffma2_rn(a2[2 * q], h2[2 * q], __fmul2_rn(du2, make_float2(bq.x, bq.y)));
+            h2[2 * q + 1] =
+                __ffma2_rn(a2[2 * q + 1], h2[2 * q + 1], __fmul2_rn(du2, make_float2(bq.z, bq.w)));
+            yq[q] = __fmul2_rn(make_float2(cq.x, cq.y), h2[2 * q]);
+            yq[q] = __ffma2_rn(make_float2(cq.z, cq.w), h2[2 * q + 1], yq[q]);
+        }
+        const float2 y2 = __fadd2_rn(yq[0], yq[1]);
+        yv[r] = y2.x + y2.y;
+    }
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void bulk_load_1d(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
 template <typename T>
 __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __grid_constant__ PFwdArgs p) {
     // Direct cast (no integer round trip): accesses stay in the shared address space.
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     PFwdSmem<T>& s = *reinterpret_cast<PFwdSmem<T>*>(smem_raw);
+    constexpr int ST = PfCfg<T>::ST;
+    constexpr bool HALF = sizeof(T) == 2;
     if ((smem_u32(smem_raw) & 127u) != 0u) {  // TMA destinations need 128-byte alignment
         if (threadIdx.x == 0) atomicCAS(p.err, 0, ERR_SMEM_ALIGN);
         return;
     }
-    const int tid = threadIdx.x;
-    const int ch = tid & (PF_CPB - 1);
-    const int half = tid >> 7;
-    const int n0 = half * 8;               // first state of this thread
+    const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
     const int total = p.nchains * p.K;
-    constexpr bool HALF = sizeof(T) == 2;
-    const unsigned stage_bytes =
-        (unsigned)((2 * PF_LT * PF_CPB + (p.has_out ? 2 : 1) * PF_LT * NSTATE) * sizeof(T));
-
-    // ---- producer (thread 0): unit queue + TMA issue --------------------------------
-    int pu = -1, ptile = 0, ptiles = 0;
-    bool pdone = false;
     auto unit_tiles = [&](int k) { return min(p.seg_tiles, p.ntiles - k * p.seg_tiles); };
-    auto issue = [&](int st) {
-        if (!pdone && (pu < 0 || ptile == ptiles)) {
-            pu = atomicAdd(p.counter, 1);
-            if (pu >= total) pdone = true;
-            ptile = 0;
-            if (!pdone) ptiles = unit_tiles(pu / p.nchains);
-        }
-        if (pdone) {
-            s.unit[st] = -1;
-            return;
-        }
-        const int c = pu % p.nchains, k = pu / p.nchains;
-        const int b = c / p.nblk, blk = c % p.nblk;
-        const int t0 = (k * p.seg_tiles + ptile) * PF_LT;
-        s.unit[st] = pu;
-        s.tile[st] = ptile;
-        mbar_expect_tx(&s.full[st], stage_bytes);
-        tma_load_3d(&s.u[st][0][0], &p.tm_u, &s.full[st], blk * PF_CPB, t0, b);
-        tma_load_3d(&s.d[st][0][0], &p.tm_d, &s.full[st], blk * PF_CPB, t0, b);
-        tma_load_3d(&s.Bt[st][0][0], &p.tm_B, &s.full[st], 0, t0, b);
-        if (p.has_out) tma_load_3d(&s.Ct[st][0][0], &p.tm_C, &s.full[st], 0, t0, b);
-        ++ptile;
-    };
 
     if (tid == 0) {
-        for (int st = 0; st < PF_ST; ++st) mbar_init(&s.full[st], 1);
+        for (int i = 0; i < ST; ++i) {
+            mbar_init(&s.full[i], 1);
+            mbar_init(&s.conv[i], 1);
+            mbar_init(&s.empty[i], PF_NCW);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&s.yfull[i], PF_NCW);
+            mbar_init(&s.yempty[i], 1);
+        }
         fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (w == PF_NCW) {
+        // ============================== producer ==============================
+        if (lane != 0) return;
         prefetch_tmap(&p.tm_u);
         prefetch_tmap(&p.tm_d);
         prefetch_tmap(&p.tm_B);
         prefetch_tmap(&p.tm_C);
-        prefetch_tmap(&p.tm_y);
-        for (int st = 0; st < PF_ST; ++st) issue(st);
+        const unsigned tile_bytes =
+            (unsigned)((2 * PF_LT * PF_CPB + (p.has_out ? 2 : 1) * PF_LT * NSTATE) * sizeof(T));
+        int pu = -1, ptile = 0, ptiles = 0;
+        for (int it = 0;; ++it) {
+            const int st = it % ST;
+            mbar_wait(&s.empty[st], ((unsigned)(it / ST) & 1u) ^ 1u, p.err);
+            if (pu < 0 || ptile == ptiles) {
+                pu = atomicAdd(p.counter, 1);
+                if (pu >= total) {
+                    s.unit[st] = -1;
+                    mbar_arrive(&s.full[st]);
+                    return;
+                }
+                ptile = 0;
+                ptiles = unit_tiles(pu / p.nchains);
+            }
+            const int c = pu % p.nchains, k = pu / p.nchains;
+            const int b = c / p.nblk, blk = c % p.nblk;
+            const int t0 = (k * p.seg_tiles + ptile) * PF_LT;
+            s.unit[st] = pu;
+            s.tile[st] = ptile;
+            unsigned bytes = tile_bytes;
+            const bool need_hand = ptile == 0 && k > 0;
+            const bool need_hprev = ptile == 0 && k == 0 && p.h_prev != nullptr;
+            const int nch = min(PF_CPB, p.D - blk * PF_CPB);
+            const unsigned rows_bytes = (unsigned)(nch * NSTATE * sizeof(T));
+            if (ptile == 0) bytes += rows_bytes + (unsigned)(nch * sizeof(T));
+            if (need_hprev) bytes += rows_bytes;
+            if (need_hand) {
+                flag_wait(&p.flags[c * p.K + k - 1], PF_NCW, p.err);
+                bytes += PF_HAND * 4;
+            }
+            mbar_expect_tx(&s.full[st], bytes);
+            if (ptile == 0) {
+                bulk_load_1d(&s.At[st][0][0], static_cast<const T*>(p.A) + (int64_t)blk * PF_CPB * NSTATE,
+                             rows_bytes, &s.full[st]);
+                bulk_load_1d(&s.Dt[st][0], static_cast<const T*>(p.Dv) + (int64_t)blk * PF_CPB,
+                             (unsigned)(nch * sizeof(T)), &s.full[st]);
+            }
+            if (need_hprev)
+                bulk_load_1d(&s.Ht[st][0][0],
+                             static_cast<const T*>(p.h_prev) + ((int64_t)b * p.D + (int64_t)blk * PF_CPB) * NSTATE,
+                             rows_bytes, &s.full[st]);
+            tma_load_3d(&s.u[st][0][0], &p.tm_u, &s.full[st], blk * PF_CPB, t0, b);
+            tma_load_3d(&s.d[st][0][0], &p.tm_d, &s.full[st], blk * PF_CPB, t0, b);
+            tma_load_3d(&s.Bt[st][0][0], &p.tm_B, &s.full[st], 0, t0, b);
+            if (p.has_out) tma_load_3d(&s.Ct[st][0][0], &p.tm_C, &s.full[st], 0, t0, b);
+            if (need_hand)
+                bulk_load_1d(&s.hin[st][0], p.hand + (int64_t)(c * p.K + k - 1) * PF_HAND,
+                             PF_HAND * 4, &s.full[st]);
+            ++ptile;
+        }
     }
-    __syncthreads();
 
-    const T* Ap = static_cast<const T*>(p.A);
-    const T* Dp = static_cast<const T*>(p.Dv);
+    if (w == PF_NCW + 1) {
+        // ============== helper: float32 B / C, TMA stores of y ==============
+        prefetch_tmap(&p.tm_y);
+        int pb = 0, pblk = 0, pt0 = 0;
+        for (int it = 0;; ++it) {
+            const int st = it % ST;
+            mbar_wait(&s.full[st], (unsigned)(it / ST) & 1u, p.err);
+            const int unit = s.unit[st];
+            int b = 0, blk = 0, t0 = 0;
+            if (unit >= 0) {
+                const int c = unit % p.nchains, k = unit / p.nchains;
+                b = c / p.nblk;
+                blk = c % p.nblk;
+                t0 = (k * p.seg_tiles + s.tile[st]) * PF_LT;
+                if constexpr (HALF) {
+                    for (int idx = lane; idx < PF_LT * NSTATE; idx += 32) {
+                        (&s.Bf[st][0][0])[idx] = to_f((&s.Bt[st][0][0])[idx]);
+                        if (p.has_out) (&s.Cf[st][0][0])[idx] = to_f((&s.Ct[st][0][0])[idx]);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s.conv[st]);
+            if (it > 0 && p.has_out) {
+                const int yb = (it - 1) & 1;
+                mbar_wait(&s.yfull[yb], (unsigned)((it - 1) / 2) & 1u, p.err);
+                if (lane == 0) {
+                    tma_store_3d(&p.tm_y, &s.y[yb][0][0], pblk * PF_CPB, pt0, pb);
+                    bulk_commit();
+                    bulk_wait_read0();
+                    mbar_arrive(&s.yempty[yb]);
+                }
+                __syncwarp();
+            }
+            if (unit < 0) break;
+            pb = b;
+            pblk = blk;
+            pt0 = t0;
+        }
+        if (lane == 0) bulk_wait0();
+        return;
+    }
+
+    // ================================ compute warps ================================
+    const int half = lane & 1;
+    const int ch = w * 16 + (lane >> 1);
+    const int n0 = half * 8;
     float2 A2v[4], h2[4];
-    float sumd = 0.f;
+    float sumd = 0.f, Dd = 0.f;
+    bool a_nonpos = true;
     int64_t d = 0;
     bool dv = false;
 
     for (int it = 0;; ++it) {
-        const int st = it % PF_ST;
-        const unsigned phase = (unsigned)(it / PF_ST) & 1u;
+        const int st = it % ST;
+        // full: the TMA bytes of this stage have landed (acquire for the async-proxy writes);
+        // conv: the helper has written the float32 B / C copies
+        mbar_wait(&s.full[st], (unsigned)(it / ST) & 1u, p.err);
+        mbar_wait(&s.conv[st], (unsigned)(it / ST) & 1u, p.err);
         const int unit = s.unit[st];
         if (unit < 0) break;
         const int tile = s.tile[st];
@@ -125,92 +270,62 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
         const int t0 = (k * p.seg_tiles + tile) * PF_LT;
         const bool last = tile == unit_tiles(k) - 1;
 
-        if (tile == 0) {  // unit start: parameters and incoming state
+        if (tile == 0) {  // unit start: parameters and incoming state (staged by the producer)
             d = (int64_t)blk * PF_CPB + ch;
             dv = d < p.D;
+            bool nonpos = true;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                A2v[j].x = dv ? to_f(Ap[d * NSTATE + n0 + 2 * j]) * LOG2E : 0.f;
-                A2v[j].y = dv ? to_f(Ap[d * NSTATE + n0 + 2 * j + 1]) * LOG2E : 0.f;
+                A2v[j].x = dv ? to_f(s.At[st][ch][n0 + 2 * j]) * LOG2E : 0.f;
+                A2v[j].y = dv ? to_f(s.At[st][ch][n0 + 2 * j + 1]) * LOG2E : 0.f;
+                nonpos = nonpos && A2v[j].x <= 0.f && A2v[j].y <= 0.f;
             }
-            if (half == 0) s.Ds[ch] = dv ? to_f(Dp[d]) : 0.f;
+            a_nonpos = __all_sync(FULL, nonpos);
+            Dd = dv ? to_f(s.Dt[st][ch]) : 0.f;
             if (k == 0) {
                 sumd = 0.f;
 #pragma unroll
                 for (int j = 0; j < 4; ++j) h2[j] = make_float2(0.f, 0.f);
                 if (p.h_prev != nullptr && dv) {
-                    const T* hp = static_cast<const T*>(p.h_prev) + ((int64_t)b * p.D + d) * NSTATE + n0;
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) h2[j] = make_float2(to_f(hp[2 * j]), to_f(hp[2 * j + 1]));
+                    for (int j = 0; j < 4; ++j)
+                        h2[j] = make_float2(to_f(s.Ht[st][ch][n0 + 2 * j]), to_f(s.Ht[st][ch][n0 + 2 * j + 1]));
                 }
             } else {
-                if (tid == 0) flag_wait(&p.flags[c * p.K + k - 1], 1, p.err);
-                __syncthreads();
-                const float* hs = p.hand + ((int64_t)(c * p.K + k - 1) * PF_CPB + ch) * (NSTATE + 1);
+                const float* hs = &s.hin[st][ch * (NSTATE + 1)];
 #pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    h2[j] = make_float2(__ldcg(hs + n0 + 2 * j), __ldcg(hs + n0 + 2 * j + 1));
-                sumd = __ldcg(hs + NSTATE);
+                for (int j = 0; j < 4; ++j) h2[j] = make_float2(hs[n0 + 2 * j], hs[n0 + 2 * j + 1]);
+                sumd = hs[NSTATE];
             }
         }
 
-        mbar_wait(&s.full[st], phase, p.err);
-        const float* Bf;
-        const float* Cf;
-        if constexpr (HALF) {
-            for (int idx = tid; idx < PF_LT * NSTATE; idx += PF_NT) {
-                (&s.Bf[0][0])[idx] = to_f((&s.Bt[st][0][0])[idx]);
-                if (p.has_out) (&s.Cf[0][0])[idx] = to_f((&s.Ct[st][0][0])[idx]);
-            }
-            __syncthreads();
-            Bf = &s.Bf[0][0];
-            Cf = &s.Cf[0][0];
-        } else {
-            Bf = reinterpret_cast<const float*>(&s.Bt[st][0][0]);
-            Cf = reinterpret_cast<const float*>(&s.Ct[st][0][0]);
-        }
+        const float* Bf = HALF ? &s.Bf[HALF ? st : 0][0][0] : reinterpret_cast<const float*>(&s.Bt[st][0][0]);
+        const float* Cf = HALF ? &s.Cf[HALF ? st : 0][0][0] : reinterpret_cast<const float*>(&s.Ct[st][0][0]);
+        const int yb = it & 1;
+        if (p.has_out) mbar_wait(&s.yempty[yb], ((unsigned)(it / 2) & 1u) ^ 1u, p.err);
 
-        // Blocks of 8 steps: the block's shared-memory reads precede its stores, and the
-        // exponent clamp of safe_exp is a branch-free min per state, so the exponentials
-        // of later steps overlap the FMAs of earlier ones.
 #pragma unroll 1
         for (int i0 = 0; i0 < PF_LT; i0 += 8) {
             float dtv[8], uv[8], yv[8];
+            float dmin = INFINITY;
 #pragma unroll
             for (int r = 0; r < 8; ++r) {
                 dtv[r] = to_f(s.d[st][i0 + r][ch]);
                 uv[r] = to_f(s.u[st][i0 + r][ch]);
+                dmin = fminf(dmin, dtv[r]);
+                sumd += dtv[r];
             }
+            if (a_nonpos && __all_sync(FULL, dmin >= 0.f))
+                fwd_block8<false>(h2, A2v, dtv, uv, Bf + i0 * NSTATE, Cf + i0 * NSTATE, n0, yv);
+            else
+                fwd_block8<true>(h2, A2v, dtv, uv, Bf + i0 * NSTATE, Cf + i0 * NSTATE, n0, yv);
+            if (p.has_out) {
 #pragma unroll
-            for (int r = 0; r < 8; ++r) {
-                const float dt = dtv[r];
-                sumd += dt;
-                const float2 dt2 = make_float2(dt, dt);
-                const float2 du2 = make_float2(dt * uv[r], dt * uv[r]);
-                float2 a2[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const float2 x = __fmul2_rn(dt2, A2v[j]);
-                    a2[j] = make_float2(ex2(fminf(x.x, ARG2_HI)), ex2(fminf(x.y, ARG2_HI)));
+                for (int r = 0; r < 8; ++r) {
+                    const float y = yv[r] + __shfl_xor_sync(FULL, yv[r], 1);
+                    if (half == 0) s.y[yb][i0 + r][ch] = from_f<T>(fmaf(Dd, uv[r], y));
                 }
-                const float4* Bq = reinterpret_cast<const float4*>(Bf + (i0 + r) * NSTATE + n0);
-                const float4* Cq = reinterpret_cast<const float4*>(Cf + (i0 + r) * NSTATE + n0);
-                float2 yq[2];
-#pragma unroll
-                for (int q = 0; q < 2; ++q) {
-                    const float4 bq = Bq[q];
-                    const float4 cq = Cq[q];
-                    h2[2 * q] = __ffma2_rn(a2[2 * q], h2[2 * q], __fmul2_rn(du2, make_float2(bq.x, bq.y)));
-                    h2[2 * q + 1] =
-                        __ffma2_rn(a2[2 * q + 1], h2[2 * q + 1], __fmul2_rn(du2, make_float2(bq.z, bq.w)));
-                    yq[q] = __fmul2_rn(make_float2(cq.x, cq.y), h2[2 * q]);
-                    yq[q] = __ffma2_rn(make_float2(cq.z, cq.w), h2[2 * q + 1], yq[q]);
-                }
-                const float2 y2 = __fadd2_rn(yq[0], yq[1]);
-                yv[r] = y2.x + y2.y;
             }
-#pragma unroll
-            for (int r = 0; r < 8; ++r) s.py[half][i0 + r][ch] = yv[r];
             if ((i0 + 8) % CK == 0 && p.ckpt != nullptr) {
                 const int64_t kk = (int64_t)(t0 + i0 + 8) / CK - 1;
                 if (kk < p.nck && dv) {
@@ -221,10 +336,18 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
                 }
             }
         }
+        // this warp is done with the stage's inputs and with its rows of the y tile
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.empty[st]);
+        if (p.has_out) {
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s.yfull[yb]);
+        }
 
         if (last) {
             if (k < p.K - 1) {
-                float* hs = p.hand + ((int64_t)(c * p.K + k) * PF_CPB + ch) * (NSTATE + 1);
+                float* hs = p.hand + (int64_t)(c * p.K + k) * PF_HAND + ch * (NSTATE + 1);
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     hs[n0 + 2 * j] = h2[j].x;
@@ -232,6 +355,8 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
                 }
                 if (half == 0) hs[NSTATE] = sumd;
                 __threadfence();
+                __syncwarp();
+                if (lane == 0) atomicAdd(&p.flags[c * p.K + k], 1);
             } else if (dv) {
                 if (p.h_last != nullptr) {
                     T* hl = static_cast<T*>(p.h_last) + ((int64_t)b * p.D + d) * NSTATE + n0;
@@ -251,38 +376,7 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
                 }
             }
         }
-
-        // y = partial(states 0-7) + partial(states 8-15) + D u, staged for the TMA store.
-        // The staging buffer of this tile was last read by the store of tile it-2.
-        if (tid == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-        __syncthreads();
-        if (p.has_out) {
-            T (*yb)[PF_CPB] = s.y[it & 1];
-#pragma unroll
-            for (int r = 0; r < (PF_LT * PF_CPB) / (4 * PF_NT); ++r) {
-                const int idx = (tid + r * PF_NT) * 4;
-                const int i = idx / PF_CPB, cc = idx % PF_CPB;
-                const float4 p0 = *reinterpret_cast<const float4*>(&s.py[0][i][cc]);
-                const float4 p1 = *reinterpret_cast<const float4*>(&s.py[1][i][cc]);
-                const float4 dd = *reinterpret_cast<const float4*>(&s.Ds[cc]);
-                yb[i][cc + 0] = from_f<T>(fmaf(dd.x, to_f(s.u[st][i][cc + 0]), p0.x + p1.x));
-                yb[i][cc + 1] = from_f<T>(fmaf(dd.y, to_f(s.u[st][i][cc + 1]), p0.y + p1.y));
-                yb[i][cc + 2] = from_f<T>(fmaf(dd.z, to_f(s.u[st][i][cc + 2]), p0.z + p1.z));
-                yb[i][cc + 3] = from_f<T>(fmaf(dd.w, to_f(s.u[st][i][cc + 3]), p0.w + p1.w));
-            }
-        }
-        fence_proxy_async();
-        __syncthreads();
-        if (tid == 0) {
-            if (p.has_out) {
-                tma_store_3d(&p.tm_y, &s.y[it & 1][0][0], blk * PF_CPB, t0, b);
-                bulk_commit();
-            }
-            if (last && k < p.K - 1) flag_release(&p.flags[c * p.K + k], 1);
-            issue(st);
-        }
     }
-    if (tid == 0) bulk_wait0();
 }
 
 // ---------------------------------------------------------------------------- host side
