@@ -237,7 +237,9 @@ int mwc_ss_bwd(const void* u, const void* delta, const void* A, const void* Bm, 
                               make_tmap_3d(&pa.tm_d, delta, dtype, D, L, B, 128, CK) &&
                               make_tmap_3d(&pa.tm_g, dout, dtype, D, L, B, 128, CK) &&
                               make_tmap_3d(&pa.tm_B, Bm, dtype, NSTATE, L, B, NSTATE, CK) &&
-                              make_tmap_3d(&pa.tm_C, Cm, dtype, NSTATE, L, B, NSTATE, CK);
+                              make_tmap_3d(&pa.tm_C, Cm, dtype, NSTATE, L, B, NSTATE, CK) &&
+                              make_tmap_3d(&pa.tm_du, du, dtype, D, L, B, 128, CK) &&
+                              make_tmap_3d(&pa.tm_dd, ddelta, dtype, D, L, B, 128, CK);
             if (maps) {
                 pa.A = A; pa.Dv = Dv; pa.h_prev = h_prev; pa.dh_last = dh_last; pa.ckpt = ckpt;
                 pa.du = du; pa.ddelta = ddelta; pa.dh_prev = dh_prev;

@@ -130,7 +130,7 @@ cudaError_t launch_fwd_persistent(PFwdArgs& a, const PersistPlan& pl, int dtype,
 
 // Persistent TMA backward (ss_bwd_tma.cu).
 struct PBwdArgs {
-    CUtensorMap tm_u, tm_d, tm_g, tm_B, tm_C;
+    CUtensorMap tm_u, tm_d, tm_g, tm_B, tm_C, tm_du, tm_dd;
     const void* A;
     const void* Dv;
     const void* h_prev;

@@ -1,25 +1,30 @@
-// Persistent, TMA-pipelined backward selective scan for sm_100a.
+// Persistent, warp-specialized, TMA-pipelined backward selective scan for sm_100a.
 //
 // Same work decomposition as the persistent forward (chains of 128 channels of one batch
 // row, cut into K time segments, taken from an atomic queue), walked in reverse: the unit
-// for the last time segment of a chain starts from dh_last, every other unit waits for the
-// adjoint state q its successor segment published (release/acquire, bounded wait).
+// for the last time segment of a chain starts from dh_last, every other unit starts from
+// the adjoint state q its successor segment published (8 per-warp increments of a flag;
+// bounded wait).
 //
 // Per 16-step tile (= one checkpoint chunk), processed last tile first:
-//   * TMA brings u, delta, dout (16 x 128), B, C (16 x 16) and, by a 1-D bulk copy, the
-//     float32 checkpoint state at the chunk start (128 x 16) into a 2-stage mbarrier ring;
-//   * the chunk's 16 states per (channel, state) are recomputed forward and kept in a
-//     per-thread shared-memory cache (conflict-free float4 layout);
-//   * the adjoint recurrence runs backwards through the chunk:
+//   * the producer warp brings u, delta, dout (16 x 128) and B, C (16 x 16) by TMA and
+//     the float32 checkpoint state at the chunk start (128 x 16) by a 1-D bulk copy into
+//     a 2-stage mbarrier ring;
+//   * 8 compute warps recompute the chunk's states forward into a per-thread shared-memory
+//     cache (conflict-free float4 layout), then run the adjoint recurrence backwards:
 //       g = dout C + q,  p = g a h_{t-1},  ddelta = ln2 <A2, p> + u <g, B>,
 //       du = dout D + delta <g, B>,  dA += delta p,  q = a g,
-//       dB_t = sum_d g delta u,  dC_t = sum_d dout h_t.
-// Thread layout: lane = (channel group cg, state group sg); a thread owns 4 adjacent
-// channels x 4 states, so the cross-channel sums of dB / dC start as in-thread FMAs and
-// finish with a 3-level butterfly over the 8 channel groups of the warp; the per-channel
-// sums <.,.> over states take 2 shuffle levels over the 4 state groups.
-// Every reduction has a fixed order (warp butterfly, warps in order, then the finalize
-// kernel over CTAs / segments / batch in order): results are bitwise reproducible.
+//       dB_t = sum_d g delta u,  dC_t = sum_d dout h_t;
+//   * the helper warp converts B / C to float32 (fp16 inputs), sums the 8 warps' dB / dC
+//     partials of a tile in warp order into the per-block workspace, and (fp16) stores the
+//     du / ddelta tiles by TMA.
+// Thread layout: warp w covers channels 16w .. 16w+15; lane = (cg, sg) with cg = lane / 4
+// the channel pair and sg = lane % 4 the state group (4 states): a thread owns 2 channels x
+// 4 states, so the cross-channel sums of dB / dC start as in-thread FMAs and finish with a
+// 3-level butterfly over the 8 channel pairs of the warp; the per-channel sums over states
+// take 2 shuffle levels. Every reduction has a fixed order (butterfly, warps in order, then
+// the finalize kernel over blocks / segments / batch rows in order): results are bitwise
+// reproducible.
 #include "mwc_device.cuh"
 #include "mwc_internal.h"
 #include "mwc_tma.cuh"
@@ -30,26 +35,38 @@ namespace mwc {
 
 constexpr int PB_LT = CK;     // 16 steps per tile
 constexpr int PB_CPB = 128;
-constexpr int PB_NT = 256;    // 8 warps: two warps per SM sub-partition
-constexpr int PB_NW = PB_NT / 32;
+constexpr int PB_NCW = 8;                    // compute warps
+constexpr int PB_NCT = PB_NCW * 32;          // compute threads
+constexpr int PB_NT = (PB_NCW + 2) * 32;     // + producer warp + helper warp
 constexpr int PB_ST = 2;
 #ifndef MWC_BWD_MIN_SEG_TILES
 #define MWC_BWD_MIN_SEG_TILES 4   // shortest segment (in 16-step tiles) the planner may pick
 #endif
 
 template <typename T>
+struct PbCfg {
+    static constexpr bool HALF = sizeof(T) == 2;
+    static constexpr int RB = HALF ? 2 : 1;       // dB | dC partial buffers
+    static constexpr bool STAGE_OUT = HALF;       // du / ddelta staged for TMA stores
+};
+
+template <typename T>
 struct __align__(128) PBwdSmem {
-    float4 hc[PB_LT][2][PB_NT];                 // state cache: [step][channel c][thread]
-    float h0[PB_ST][PB_CPB][NSTATE];            // checkpoint at the chunk start
+    using C = PbCfg<T>;
+    float4 hc[PB_LT][2][PB_NCT];                 // state cache: [step][channel c][thread]
+    float h0[PB_ST][PB_CPB][NSTATE];             // checkpoint at the chunk start
     T u[PB_ST][PB_LT][PB_CPB];
     T d[PB_ST][PB_LT][PB_CPB];
     T g[PB_ST][PB_LT][PB_CPB];
     T Bt[PB_ST][PB_LT][NSTATE];
     T Ct[PB_ST][PB_LT][NSTATE];
-    float red[PB_NW][PB_LT][2 * NSTATE];        // per-warp dB | dC partials of the tile
-    float Bf[PB_LT][NSTATE];                    // float32 copies of B / C (fp16 inputs)
-    float Cf[PB_LT][NSTATE];
-    uint64_t full[PB_ST];
+    T duo[C::STAGE_OUT ? 2 : 1][C::STAGE_OUT ? PB_LT : 1][C::STAGE_OUT ? PB_CPB : 8];  // du / ddelta
+    T ddo[C::STAGE_OUT ? 2 : 1][C::STAGE_OUT ? PB_LT : 1][C::STAGE_OUT ? PB_CPB : 8];  // staging
+    float red[C::RB][PB_NCW][PB_LT][2 * NSTATE];  // per-warp dB | dC partials of a tile
+    float Bf[C::HALF ? PB_ST : 1][PB_LT][NSTATE];
+    float Cf[C::HALF ? PB_ST : 1][PB_LT][NSTATE];
+    uint64_t full[PB_ST], conv[PB_ST], empty[PB_ST];
+    uint64_t redfull[C::RB], redempty[C::RB], ofull[2], oempty[2];
     int unit[PB_ST];
     int tile[PB_ST];
 };
@@ -60,6 +77,10 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, unsigned b
             smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_b(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 template <typename T>
@@ -119,88 +140,170 @@ __device__ __forceinline__ void store4<__half>(__half* p, const float (&v)[4]) {
 
 __device__ __forceinline__ float2 f2(float x) { return make_float2(x, x); }
 
-// Thread layout: warp w covers channels 16w .. 16w+15; lane = (cg, sg) with cg = lane / 4
-// the channel pair (2 adjacent channels) and sg = lane % 4 the state group (4 states).
 template <typename T>
 __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __grid_constant__ PBwdArgs p) {
     // Direct cast (no integer round trip): accesses stay in the shared address space.
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     PBwdSmem<T>& s = *reinterpret_cast<PBwdSmem<T>*>(smem_raw);
+    using Cfg = PbCfg<T>;
+    constexpr bool HALF = Cfg::HALF;
+    constexpr int RB = Cfg::RB;
     if ((smem_u32(smem_raw) & 127u) != 0u) {  // TMA destinations need 128-byte alignment
         if (threadIdx.x == 0) atomicCAS(p.err, 0, ERR_SMEM_ALIGN);
         return;
     }
-    constexpr bool HALF = sizeof(T) == 2;
     const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
-    const int cg = lane >> 2, sg = lane & 3;
-    const int c2 = w * 16 + cg * 2;          // first of the thread's 2 channels in the block
     const int total = p.nchains * p.K;
     const int64_t Lp = (int64_t)p.nck * CK;
-    const unsigned tile_bytes = (unsigned)((3 * PB_LT * PB_CPB + 2 * PB_LT * NSTATE) * sizeof(T));
-
-    // ---- producer (thread 0) -------------------------------------------------------
-    int pu = -1, pcount = 0, ptiles = 0, pfirst = 0;
-    bool pdone = false;
-    auto issue = [&](int st) {
-        if (!pdone && (pu < 0 || pcount == ptiles)) {
-            pu = atomicAdd(p.counter, 1);
-            if (pu >= total) {
-                pdone = true;
-            } else {
-                const int k = p.K - 1 - pu / p.nchains;
-                pfirst = k * p.seg_tiles;
-                ptiles = min(p.seg_tiles, p.ntiles - pfirst);
-                pcount = 0;
-            }
-        }
-        if (pdone) {
-            s.unit[st] = -1;
-            return;
-        }
-        const int c = pu % p.nchains;
-        const int b = c / p.nblk, blk = c % p.nblk;
-        const int tix = pfirst + ptiles - 1 - pcount;
-        const int t0 = tix * PB_LT;
-        s.unit[st] = pu;
-        s.tile[st] = pcount;
-        const int nch = min(PB_CPB, p.D - blk * PB_CPB);
-        const unsigned hbytes = tix > 0 ? (unsigned)(nch * NSTATE * 4) : 0u;
-        mbar_expect_tx(&s.full[st], tile_bytes + hbytes);
-        tma_load_3d(&s.u[st][0][0], &p.tm_u, &s.full[st], blk * PB_CPB, t0, b);
-        tma_load_3d(&s.d[st][0][0], &p.tm_d, &s.full[st], blk * PB_CPB, t0, b);
-        tma_load_3d(&s.g[st][0][0], &p.tm_g, &s.full[st], blk * PB_CPB, t0, b);
-        tma_load_3d(&s.Bt[st][0][0], &p.tm_B, &s.full[st], 0, t0, b);
-        tma_load_3d(&s.Ct[st][0][0], &p.tm_C, &s.full[st], 0, t0, b);
-        if (tix > 0)
-            bulk_load(&s.h0[st][0][0],
-                      p.ckpt + (((int64_t)b * p.nck + tix - 1) * p.D + (int64_t)blk * PB_CPB) * NSTATE,
-                      hbytes, &s.full[st]);
-        ++pcount;
-    };
 
     if (tid == 0) {
-        for (int st = 0; st < PB_ST; ++st) mbar_init(&s.full[st], 1);
+        for (int i = 0; i < PB_ST; ++i) {
+            mbar_init(&s.full[i], 1);
+            mbar_init(&s.conv[i], 1);
+            mbar_init(&s.empty[i], PB_NCW);
+        }
+        for (int i = 0; i < RB; ++i) {
+            mbar_init(&s.redfull[i], PB_NCW);
+            mbar_init(&s.redempty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&s.ofull[i], PB_NCW);
+            mbar_init(&s.oempty[i], 1);
+        }
         fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (w == PB_NCW) {
+        // ============================== producer ==============================
+        if (lane != 0) return;
         prefetch_tmap(&p.tm_u);
         prefetch_tmap(&p.tm_d);
         prefetch_tmap(&p.tm_g);
         prefetch_tmap(&p.tm_B);
         prefetch_tmap(&p.tm_C);
-        for (int st = 0; st < PB_ST; ++st) issue(st);
+        const unsigned tile_bytes = (unsigned)((3 * PB_LT * PB_CPB + 2 * PB_LT * NSTATE) * sizeof(T));
+        int pu = -1, pcount = 0, ptiles = 0, pfirst = 0;
+        for (int it = 0;; ++it) {
+            const int st = it % PB_ST;
+            mbar_wait(&s.empty[st], ((unsigned)(it / PB_ST) & 1u) ^ 1u, p.err);
+            if (pu < 0 || pcount == ptiles) {
+                pu = atomicAdd(p.counter, 1);
+                if (pu >= total) {
+                    s.unit[st] = -1;
+                    mbar_arrive_b(&s.full[st]);
+                    return;
+                }
+                const int k = p.K - 1 - pu / p.nchains;
+                pfirst = k * p.seg_tiles;
+                ptiles = min(p.seg_tiles, p.ntiles - pfirst);
+                pcount = 0;
+            }
+            const int c = pu % p.nchains, kp = pu / p.nchains;
+            const int b = c / p.nblk, blk = c % p.nblk;
+            const int tix = pfirst + ptiles - 1 - pcount;
+            const int t0 = tix * PB_LT;
+            s.unit[st] = pu;
+            s.tile[st] = pcount;
+            // the successor segment's adjoint state must be published before the unit's
+            // compute warps read it (they read it after this stage's barrier completes)
+            if (pcount == 0 && kp > 0) flag_wait(&p.flags[c * p.K + kp - 1], PB_NCW, p.err);
+            const int nch = min(PB_CPB, p.D - blk * PB_CPB);
+            const unsigned hbytes = tix > 0 ? (unsigned)(nch * NSTATE * 4) : 0u;
+            mbar_expect_tx(&s.full[st], tile_bytes + hbytes);
+            tma_load_3d(&s.u[st][0][0], &p.tm_u, &s.full[st], blk * PB_CPB, t0, b);
+            tma_load_3d(&s.d[st][0][0], &p.tm_d, &s.full[st], blk * PB_CPB, t0, b);
+            tma_load_3d(&s.g[st][0][0], &p.tm_g, &s.full[st], blk * PB_CPB, t0, b);
+            tma_load_3d(&s.Bt[st][0][0], &p.tm_B, &s.full[st], 0, t0, b);
+            tma_load_3d(&s.Ct[st][0][0], &p.tm_C, &s.full[st], 0, t0, b);
+            if (tix > 0)
+                bulk_load(&s.h0[st][0][0],
+                          p.ckpt + (((int64_t)b * p.nck + tix - 1) * p.D + (int64_t)blk * PB_CPB) * NSTATE,
+                          hbytes, &s.full[st]);
+            ++pcount;
+        }
     }
-    __syncthreads();
 
+    if (w == PB_NCW + 1) {
+        // ======= helper: float32 B / C, ordered dB | dC partials, du / ddelta stores =======
+        if constexpr (Cfg::STAGE_OUT) {
+            prefetch_tmap(&p.tm_du);
+            prefetch_tmap(&p.tm_dd);
+        }
+        int pb = 0, pblk = 0, pt0 = 0;
+        for (int it = 0;; ++it) {
+            const int st = it % PB_ST;
+            mbar_wait(&s.full[st], (unsigned)(it / PB_ST) & 1u, p.err);
+            const int unit = s.unit[st];
+            int b = 0, blk = 0, t0 = 0;
+            if (unit >= 0) {
+                const int c = unit % p.nchains, kp = unit / p.nchains, k = p.K - 1 - kp;
+                b = c / p.nblk;
+                blk = c % p.nblk;
+                const int first = k * p.seg_tiles;
+                const int ntl = min(p.seg_tiles, p.ntiles - first);
+                t0 = (first + ntl - 1 - s.tile[st]) * PB_LT;
+                if constexpr (HALF) {
+                    for (int idx = lane; idx < PB_LT * NSTATE; idx += 32) {
+                        (&s.Bf[HALF ? st : 0][0][0])[idx] = to_f((&s.Bt[st][0][0])[idx]);
+                        (&s.Cf[HALF ? st : 0][0][0])[idx] = to_f((&s.Ct[st][0][0])[idx]);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive_b(&s.conv[st]);
+            if (it > 0) {
+                const int rb = (it - 1) % RB;
+                mbar_wait(&s.redfull[rb], (unsigned)((it - 1) / RB) & 1u, p.err);
+                float* wb = p.ws_bc + (((int64_t)pblk * p.B + pb) * Lp + pt0) * (2 * NSTATE);
+#pragma unroll 4
+                for (int r = 0; r < (PB_LT * 2 * NSTATE) / 32; ++r) {
+                    const int idx = lane + r * 32;
+                    const int i = idx / (2 * NSTATE), vv = idx % (2 * NSTATE);
+                    float acc = s.red[rb][0][i][vv];
+#pragma unroll
+                    for (int ww = 1; ww < PB_NCW; ++ww) acc += s.red[rb][ww][i][vv];
+                    wb[idx] = acc;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive_b(&s.redempty[rb]);
+                if constexpr (Cfg::STAGE_OUT) {
+                    const int ob = (it - 1) & 1;
+                    mbar_wait(&s.ofull[ob], (unsigned)((it - 1) / 2) & 1u, p.err);
+                    if (lane == 0) {
+                        tma_store_3d(&p.tm_du, &s.duo[ob][0][0], pblk * PB_CPB, pt0, pb);
+                        tma_store_3d(&p.tm_dd, &s.ddo[ob][0][0], pblk * PB_CPB, pt0, pb);
+                        bulk_commit();
+                        bulk_wait_read0();
+                        mbar_arrive_b(&s.oempty[ob]);
+                    }
+                    __syncwarp();
+                }
+            }
+            if (unit < 0) break;
+            pb = b;
+            pblk = blk;
+            pt0 = t0;
+        }
+        if (lane == 0) bulk_wait0();
+        return;
+    }
+
+    // ================================ compute warps ================================
+    const int cg = lane >> 2, sg = lane & 3;
+    const int c2 = w * 16 + cg * 2;          // first of the thread's 2 channels in the block
     const T* Ap = static_cast<const T*>(p.A);
     const T* Dp = static_cast<const T*>(p.Dv);
     float2 A2[2][2], q[2][2], dA[2][2];
     float Dd[2], dD[2];
     bool a_nonpos = true;   // warp-uniform: A <= 0, so delta >= 0 keeps every exponent <= 0
-    int64_t dbase = 0;                      // first of the 2 channels (global index)
+    int64_t dbase = 0;
     const int oidx = (cg < 4) ? (4 * sg + cg) : (NSTATE + 4 * sg + cg - 4);
 
     for (int it = 0;; ++it) {
         const int st = it % PB_ST;
-        const unsigned phase = (unsigned)(it / PB_ST) & 1u;
+        mbar_wait(&s.full[st], (unsigned)(it / PB_ST) & 1u, p.err);
+        mbar_wait(&s.conv[st], (unsigned)(it / PB_ST) & 1u, p.err);
         const int unit = s.unit[st];
         if (unit < 0) break;
 
@@ -241,8 +344,6 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                     q[cc][1] = make_float2(g4[2], g4[3]);
                 }
             } else {
-                if (tid == 0) flag_wait(&p.flags[c * p.K + kp - 1], 1, p.err);
-                __syncthreads();
                 const float* hs = p.hand + ((int64_t)(c * p.K + kp - 1) * PB_CPB + c2) * NSTATE + 4 * sg;
 #pragma unroll
                 for (int cc = 0; cc < 2; ++cc) {
@@ -253,17 +354,8 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
             }
         }
 
-        mbar_wait(&s.full[st], phase, p.err);
-        if constexpr (HALF) {
-            for (int idx = tid; idx < PB_LT * NSTATE; idx += PB_NT) {
-                (&s.Bf[0][0])[idx] = to_f((&s.Bt[st][0][0])[idx]);
-                (&s.Cf[0][0])[idx] = to_f((&s.Ct[st][0][0])[idx]);
-            }
-        }
-        // also orders the previous tile's reads of red before this tile's writes
-        __syncthreads();
-        const float* Bf = HALF ? &s.Bf[0][0] : reinterpret_cast<const float*>(&s.Bt[st][0][0]);
-        const float* Cf = HALF ? &s.Cf[0][0] : reinterpret_cast<const float*>(&s.Ct[st][0][0]);
+        const float* Bf = HALF ? &s.Bf[HALF ? st : 0][0][0] : reinterpret_cast<const float*>(&s.Bt[st][0][0]);
+        const float* Cf = HALF ? &s.Cf[HALF ? st : 0][0][0] : reinterpret_cast<const float*>(&s.Ct[st][0][0]);
 
         // state at the chunk start
         float2 h[2][2];
@@ -343,6 +435,10 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
         }
 
         // ---- adjoint pass -------------------------------------------------------------
+        const int rb = it % RB;
+        mbar_wait(&s.redempty[rb], ((unsigned)(it / RB) & 1u) ^ 1u, p.err);
+        const int ob = it & 1;
+        if constexpr (Cfg::STAGE_OUT) mbar_wait(&s.oempty[ob], ((unsigned)(it / 2) & 1u) ^ 1u, p.err);
         T* dub = static_cast<T*>(p.du);
         T* ddb = static_cast<T*>(p.ddelta);
         float2 ht[2][2];
@@ -432,20 +528,27 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                     v[j] = keep + __shfl_xor_sync(FULL, send, m * 4);
                 }
             }
-            s.red[w][i][oidx] = v[0];
-            const int t = t0 + i;
-            if (sg == 0 && t < p.L) {
+            s.red[rb][w][i][oidx] = v[0];
+            if (sg == 0) {
                 const float du0 = fmaf(gy[0], Dd[0], dt[0] * S2[0]);
                 const float du1 = fmaf(gy[1], Dd[1], dt[1] * S2[1]);
                 const float dd0 = fmaf(uu[0], S2[0], S1[0] * LN2);
                 const float dd1 = fmaf(uu[1], S2[1], S1[1] * LN2);
-                const int64_t off = ((int64_t)b * p.L + t) * p.D + dbase;
-                if (dvc[1]) {
-                    store2<T>(dub + off, du0, du1);
-                    store2<T>(ddb + off, dd0, dd1);
-                } else if (dvc[0]) {
-                    dub[off] = from_f<T>(du0);
-                    ddb[off] = from_f<T>(dd0);
+                if constexpr (Cfg::STAGE_OUT) {
+                    store2<T>(&s.duo[ob][i][c2], du0, du1);
+                    store2<T>(&s.ddo[ob][i][c2], dd0, dd1);
+                } else {
+                    const int t = t0 + i;
+                    if (t < p.L) {
+                        const int64_t off = ((int64_t)b * p.L + t) * p.D + dbase;
+                        if (dvc[1]) {
+                            store2<T>(dub + off, du0, du1);
+                            store2<T>(ddb + off, dd0, dd1);
+                        } else if (dvc[0]) {
+                            dub[off] = from_f<T>(du0);
+                            ddb[off] = from_f<T>(dd0);
+                        }
+                    }
                 }
             }
 #pragma unroll
@@ -453,6 +556,17 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                 ht[cc][0] = hp[cc][0];
                 ht[cc][1] = hp[cc][1];
             }
+        }
+        // inputs of the stage consumed; partials and output tile written
+        __syncwarp();
+        if (lane == 0) {
+            mbar_arrive_b(&s.empty[st]);
+            mbar_arrive_b(&s.redfull[rb]);
+        }
+        if constexpr (Cfg::STAGE_OUT) {
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_b(&s.ofull[ob]);
         }
 
         if (unit_end) {
@@ -469,6 +583,8 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                     *reinterpret_cast<float4*>(hs + cc * NSTATE) =
                         make_float4(q[cc][0].x, q[cc][0].y, q[cc][1].x, q[cc][1].y);
                 __threadfence();
+                __syncwarp();
+                if (lane == 0) atomicAdd(&p.flags[c * p.K + kp], 1);
             } else if (p.dh_prev != nullptr) {
 #pragma unroll
                 for (int cc = 0; cc < 2; ++cc)
@@ -477,24 +593,6 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                         store4<T>(static_cast<T*>(p.dh_prev) + ((int64_t)b * p.D + dbase + cc) * NSTATE + 4 * sg, v4);
                     }
             }
-        }
-        __syncthreads();
-        // dB | dC partials of this tile: the 8 warps summed in order, one row per step
-        {
-            float* wb = p.ws_bc + (((int64_t)blk * p.B + b) * Lp + t0) * (2 * NSTATE);
-#pragma unroll
-            for (int r = 0; r < (PB_LT * 2 * NSTATE) / PB_NT; ++r) {
-                const int idx = tid + r * PB_NT;
-                const int i = idx / (2 * NSTATE), vv = idx % (2 * NSTATE);
-                float acc = s.red[0][i][vv];
-#pragma unroll
-                for (int ww = 1; ww < PB_NW; ++ww) acc += s.red[ww][i][vv];
-                wb[idx] = acc;
-            }
-        }
-        if (tid == 0) {
-            if (unit_end && k > 0) flag_release(&p.flags[c * p.K + kp], 1);
-            issue(st);
         }
     }
 }
