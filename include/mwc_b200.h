@@ -127,6 +127,24 @@ MWC_API int mwc_lin_scan_fwd(const void* a, const void* x, void* h, int64_t R, i
 MWC_API int mwc_lin_scan_bwd(const void* a, const void* h, const void* g, void* ga, void* gx,
                      int64_t R, int64_t L, int64_t N, int dtype, void* stream);
 
+/*
+ * mwc_ss_fwd_noalloc -- the forward scan of mwc_ss_fwd (same arguments, same results) for
+ * callers that cannot allocate device memory, such as foreign-language bindings that only
+ * own their input and output buffers, or latency-bound loops where cudaMalloc's implicit
+ * synchronization is not acceptable. It takes no workspace: the L-segment carries live in a
+ * file-scope device array of 4 MiB that every GPU loading the library keeps until exit; a
+ * shape that would need more is rejected with MWC_ERR_UNSUPPORTED. The first call on a device
+ * looks up the array's address (make it before any stream capture). All calls on a device
+ * share the array; each call rewrites what it reads, but calls that overlap on the GPU race.
+ * Always runs the segmented forward kernels (never the persistent TMA kernel, whose
+ * workspace grows with B*D). No counterpart in the reference: its ops always allocated
+ * their outputs and scratch through the PyTorch allocator.
+ */
+MWC_API int mwc_ss_fwd_noalloc(const void* u, const void* delta, const void* A, const void* Bm,
+                               const void* Cm, const void* Dv, const void* h_prev, void* out,
+                               void* h_last, float* ckpt, float* decay,
+                               int64_t B, int64_t L, int64_t D, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -95,6 +95,16 @@ int check_sizes(int64_t B, int64_t L, int64_t D) {
 
 }  // namespace
 
+namespace mwc {
+// Error reporting for entry points defined in other files of the library.
+int report_error(int code, const char* msg) {
+    snprintf(g_err, sizeof(g_err), "%s", msg);
+    return code;
+}
+int report_ok() { return ok(); }
+int current_device_sms() { return device_sms(); }
+}  // namespace mwc
+
 extern "C" {
 
 int mwc_abi_version(void) { return MWC_ABI_VERSION; }

@@ -159,6 +159,11 @@ BwdPersistWs bwd_persistent_ws(const PersistPlan& pl, int64_t B, int64_t L);
 cudaError_t launch_bwd_persistent(PBwdArgs& a, const PersistPlan& pl, int dtype, void* ws,
                                   void* dA, void* dB, void* dC, void* dD, cudaStream_t s);
 
+// Error reporting shared by the C entry points (capi.cu).
+int report_error(int code, const char* msg);
+int report_ok();
+int current_device_sms();
+
 // Launch-shape descriptors chosen by the host heuristics in capi.cu.
 struct FwdPlan {
     int states_per_thread;  // 16, 8 or 4
