@@ -298,7 +298,6 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
     float Dd[2], dD[2];
     bool a_nonpos = true;   // warp-uniform: A <= 0, so delta >= 0 keeps every exponent <= 0
     int64_t dbase = 0;
-    const int oidx = (cg < 4) ? (4 * sg + cg) : (NSTATE + 4 * sg + cg - 4);
 
     for (int it = 0;; ++it) {
         const int st = it % PB_ST;
@@ -357,29 +356,26 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
         const float* Bf = HALF ? &s.Bf[HALF ? st : 0][0][0] : reinterpret_cast<const float*>(&s.Bt[st][0][0]);
         const float* Cf = HALF ? &s.Cf[HALF ? st : 0][0][0] : reinterpret_cast<const float*>(&s.Ct[st][0][0]);
 
-        // state at the chunk start
+        // state at the chunk start (channels past D stay zero)
         float2 h[2][2];
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
             float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (tix > 0) {
-                v = *reinterpret_cast<const float4*>(&s.h0[st][c2 + cc][4 * sg]);
-            } else if (p.h_prev != nullptr && dvc[cc]) {
-                float hp4[4];
-                load4<T>(hp4, static_cast<const T*>(p.h_prev) + ((int64_t)b * p.D + dbase + cc) * NSTATE + 4 * sg);
-                v = make_float4(hp4[0], hp4[1], hp4[2], hp4[3]);
+            if (dvc[cc]) {
+                if (tix > 0) {
+                    v = *reinterpret_cast<const float4*>(&s.h0[st][c2 + cc][4 * sg]);
+                } else if (p.h_prev != nullptr) {
+                    float hp4[4];
+                    load4<T>(hp4, static_cast<const T*>(p.h_prev) + ((int64_t)b * p.D + dbase + cc) * NSTATE + 4 * sg);
+                    v = make_float4(hp4[0], hp4[1], hp4[2], hp4[3]);
+                }
             }
             h[cc][0] = make_float2(v.x, v.y);
             h[cc][1] = make_float2(v.z, v.w);
         }
-        float2 h0[2][2];
-#pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-            h0[cc][0] = h[cc][0];
-            h0[cc][1] = h[cc][1];
-        }
 
-        // ---- recompute the chunk's states (blocks of 4 steps: loads, then stores) ----
+        // ---- recompute: hc[i] = state before step i; h ends as the state after the last
+        //      step (blocks of 4 steps: loads, then the serial updates) ----
 #pragma unroll 1
         for (int i0 = 0; i0 < PB_LT; i0 += 4) {
             float dt[4][2], uu[4][2];
@@ -390,7 +386,6 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                 load2<T>(uu[r], &s.u[st][i0 + r][c2]);
                 B4[r] = *reinterpret_cast<const float4*>(Bf + (i0 + r) * NSTATE + 4 * sg);
             }
-            float4 hv[4][2];
             float dmin = INFINITY;
 #pragma unroll
             for (int r = 0; r < 4; ++r) dmin = fminf(dmin, fminf(dt[r][0], dt[r][1]));
@@ -419,121 +414,135 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                 const float2 Bp0 = make_float2(B4[r].x, B4[r].y), Bp1 = make_float2(B4[r].z, B4[r].w);
 #pragma unroll
                 for (int cc = 0; cc < 2; ++cc) {
+                    s.hc[i0 + r][cc][tid] = make_float4(h[cc][0].x, h[cc][0].y, h[cc][1].x, h[cc][1].y);
                     const float2 du2 = f2(dt[r][cc] * uu[r][cc]);
                     const float2 a0 = make_float2(ex2(x[r][cc][0].x), ex2(x[r][cc][0].y));
                     const float2 a1 = make_float2(ex2(x[r][cc][1].x), ex2(x[r][cc][1].y));
                     h[cc][0] = __ffma2_rn(a0, h[cc][0], __fmul2_rn(du2, Bp0));
                     h[cc][1] = __ffma2_rn(a1, h[cc][1], __fmul2_rn(du2, Bp1));
-                    hv[r][cc] = make_float4(h[cc][0].x, h[cc][0].y, h[cc][1].x, h[cc][1].y);
                 }
-            }
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                s.hc[i0 + r][0][tid] = hv[r][0];
-                s.hc[i0 + r][1][tid] = hv[r][1];
             }
         }
 
-        // ---- adjoint pass -------------------------------------------------------------
+        // ---- adjoint pass: blocks of 4 steps, last block first. The serial updates run
+        //      step by step; the cross-lane sums of a block are batched after it ----
         const int rb = it % RB;
         mbar_wait(&s.redempty[rb], ((unsigned)(it / RB) & 1u) ^ 1u, p.err);
         const int ob = it & 1;
         if constexpr (Cfg::STAGE_OUT) mbar_wait(&s.oempty[ob], ((unsigned)(it / 2) & 1u) ^ 1u, p.err);
         T* dub = static_cast<T*>(p.du);
         T* ddb = static_cast<T*>(p.ddelta);
-        float2 ht[2][2];
+        float2 ht[2][2];   // state after the step being processed
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
             ht[cc][0] = h[cc][0];
             ht[cc][1] = h[cc][1];
         }
 #pragma unroll 1
-        for (int i = PB_LT - 1; i >= 0; --i) {
-            float dt[2], uu[2], gy[2];
-            load2<T>(dt, &s.d[st][i][c2]);
-            load2<T>(uu, &s.u[st][i][c2]);
-            load2<T>(gy, &s.g[st][i][c2]);
-            const float4 B4 = *reinterpret_cast<const float4*>(Bf + i * NSTATE + 4 * sg);
-            const float4 C4 = *reinterpret_cast<const float4*>(Cf + i * NSTATE + 4 * sg);
-            const float2 Bp[2] = {make_float2(B4.x, B4.y), make_float2(B4.z, B4.w)};
-            const float2 Cp[2] = {make_float2(C4.x, C4.y), make_float2(C4.z, C4.w)};
-            float2 hp[2][2];
+        for (int i0 = PB_LT - 4; i0 >= 0; i0 -= 4) {
+            float dt[4][2], uu[4][2], gy[4][2];
 #pragma unroll
-            for (int cc = 0; cc < 2; ++cc) {
-                if (i > 0) {
-                    const float4 v = s.hc[i - 1][cc][tid];
-                    hp[cc][0] = make_float2(v.x, v.y);
-                    hp[cc][1] = make_float2(v.z, v.w);
-                } else {
-                    hp[cc][0] = h0[cc][0];
-                    hp[cc][1] = h0[cc][1];
-                }
+            for (int r = 0; r < 4; ++r) {
+                load2<T>(dt[r], &s.d[st][i0 + r][c2]);
+                load2<T>(uu[r], &s.u[st][i0 + r][c2]);
+                load2<T>(gy[r], &s.g[st][i0 + r][c2]);
             }
-            float2 vB[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-            float2 vC[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-            float S1[2], S2[2];
-            float2 x[2][2];
+            float dmin = INFINITY;
 #pragma unroll
-            for (int cc = 0; cc < 2; ++cc) {
-                x[cc][0] = __fmul2_rn(f2(dt[cc]), A2[cc][0]);
-                x[cc][1] = __fmul2_rn(f2(dt[cc]), A2[cc][1]);
-            }
-            if (!(a_nonpos && __all_sync(FULL, dt[0] >= 0.f && dt[1] >= 0.f))) {
+            for (int r = 0; r < 4; ++r) dmin = fminf(dmin, fminf(dt[r][0], dt[r][1]));
+            const bool fast = a_nonpos && __all_sync(FULL, dmin >= 0.f);
+            float vv[4][8];   // per step: dB partial (states 4sg..4sg+3), then dC partial
+            float sv[4][4];   // per step: S1 (channels c2, c2+1), then S2
 #pragma unroll
-                for (int cc = 0; cc < 2; ++cc)
-#pragma unroll
-                    for (int pr = 0; pr < 2; ++pr)
-                        x[cc][pr] = make_float2(fminf(x[cc][pr].x, ARG2_HI), fminf(x[cc][pr].y, ARG2_HI));
-            }
-#pragma unroll
-            for (int cc = 0; cc < 2; ++cc) {
-                const float2 dt2 = f2(dt[cc]);
-                const float2 du2 = f2(dt[cc] * uu[cc]);
-                const float2 gy2 = f2(gy[cc]);
-                float2 s1 = make_float2(0.f, 0.f), s2 = make_float2(0.f, 0.f);
-#pragma unroll
-                for (int pr = 0; pr < 2; ++pr) {
-                    const float2 a = make_float2(ex2(x[cc][pr].x), ex2(x[cc][pr].y));
-                    const float2 g = __ffma2_rn(gy2, Cp[pr], q[cc][pr]);
-                    const float2 pp = __fmul2_rn(g, __fmul2_rn(a, hp[cc][pr]));
-                    s1 = __ffma2_rn(A2[cc][pr], pp, s1);
-                    dA[cc][pr] = __ffma2_rn(dt2, pp, dA[cc][pr]);
-                    s2 = __ffma2_rn(g, Bp[pr], s2);
-                    vB[pr] = __ffma2_rn(g, du2, vB[pr]);
-                    vC[pr] = __ffma2_rn(gy2, ht[cc][pr], vC[pr]);
-                    q[cc][pr] = __fmul2_rn(a, g);
-                }
-                S1[cc] = s1.x + s1.y;
-                S2[cc] = s2.x + s2.y;
-                dD[cc] = fmaf(gy[cc], uu[cc], dD[cc]);
-            }
-            // per-channel sums over the 4 state groups (xor 1, 2)
-#pragma unroll
-            for (int o = 1; o <= 2; o <<= 1) {
+            for (int r = 3; r >= 0; --r) {
+                const int i = i0 + r;
+                const float4 B4 = *reinterpret_cast<const float4*>(Bf + i * NSTATE + 4 * sg);
+                const float4 C4 = *reinterpret_cast<const float4*>(Cf + i * NSTATE + 4 * sg);
+                const float2 Bp[2] = {make_float2(B4.x, B4.y), make_float2(B4.z, B4.w)};
+                const float2 Cp[2] = {make_float2(C4.x, C4.y), make_float2(C4.z, C4.w)};
+                float2 hp[2][2];   // state before step i
 #pragma unroll
                 for (int cc = 0; cc < 2; ++cc) {
-                    S1[cc] += __shfl_xor_sync(FULL, S1[cc], o);
-                    S2[cc] += __shfl_xor_sync(FULL, S2[cc], o);
+                    const float4 v = s.hc[i][cc][tid];
+                    hp[cc][0] = make_float2(v.x, v.y);
+                    hp[cc][1] = make_float2(v.z, v.w);
+                }
+                float2 x[2][2];
+#pragma unroll
+                for (int cc = 0; cc < 2; ++cc) {
+                    x[cc][0] = __fmul2_rn(f2(dt[r][cc]), A2[cc][0]);
+                    x[cc][1] = __fmul2_rn(f2(dt[r][cc]), A2[cc][1]);
+                }
+                if (!fast) {
+#pragma unroll
+                    for (int cc = 0; cc < 2; ++cc)
+#pragma unroll
+                        for (int pr = 0; pr < 2; ++pr)
+                            x[cc][pr] = make_float2(fminf(x[cc][pr].x, ARG2_HI), fminf(x[cc][pr].y, ARG2_HI));
+                }
+                float2 vB[2], vC[2];
+#pragma unroll
+                for (int cc = 0; cc < 2; ++cc) {
+                    const float2 dt2 = f2(dt[r][cc]);
+                    const float2 du2 = f2(dt[r][cc] * uu[r][cc]);
+                    const float2 gy2 = f2(gy[r][cc]);
+                    float2 s1, s2;
+#pragma unroll
+                    for (int pr = 0; pr < 2; ++pr) {
+                        const float2 a = make_float2(ex2(x[cc][pr].x), ex2(x[cc][pr].y));
+                        const float2 g = __ffma2_rn(gy2, Cp[pr], q[cc][pr]);
+                        const float2 pp = __fmul2_rn(g, __fmul2_rn(a, hp[cc][pr]));
+                        s1 = pr == 0 ? __fmul2_rn(A2[cc][pr], pp) : __ffma2_rn(A2[cc][pr], pp, s1);
+                        s2 = pr == 0 ? __fmul2_rn(g, Bp[pr]) : __ffma2_rn(g, Bp[pr], s2);
+                        dA[cc][pr] = __ffma2_rn(dt2, pp, dA[cc][pr]);
+                        vB[pr] = cc == 0 ? __fmul2_rn(g, du2) : __ffma2_rn(g, du2, vB[pr]);
+                        vC[pr] = cc == 0 ? __fmul2_rn(gy2, ht[cc][pr]) : __ffma2_rn(gy2, ht[cc][pr], vC[pr]);
+                        q[cc][pr] = __fmul2_rn(a, g);
+                    }
+                    sv[r][cc] = s1.x + s1.y;
+                    sv[r][2 + cc] = s2.x + s2.y;
+                    dD[cc] = fmaf(gy[r][cc], uu[r][cc], dD[cc]);
+                }
+                vv[r][0] = vB[0].x; vv[r][1] = vB[0].y; vv[r][2] = vB[1].x; vv[r][3] = vB[1].y;
+                vv[r][4] = vC[0].x; vv[r][5] = vC[0].y; vv[r][6] = vC[1].x; vv[r][7] = vC[1].y;
+#pragma unroll
+                for (int cc = 0; cc < 2; ++cc) {
+                    ht[cc][0] = hp[cc][0];
+                    ht[cc][1] = hp[cc][1];
                 }
             }
-            // dB | dC over the warp's 8 channel pairs: reduce-scatter (xor 16, 8, 4)
-            float v[8] = {vB[0].x, vB[0].y, vB[1].x, vB[1].y, vC[0].x, vC[0].y, vC[1].x, vC[1].y};
+            // S1 / S2 over the 4 state groups: reduce-scatter (xor 2, then 1); lane sg
+            // ends with the sums of step i0 + sg
+            {
+                const bool up = (sg & 2) != 0;
 #pragma unroll
-            for (int m = 4; m >= 1; m >>= 1) {
-                const bool up = (cg & m) != 0;
+                for (int r = 0; r < 2; ++r)
 #pragma unroll
-                for (int j = 0; j < m; ++j) {
-                    const float send = up ? v[j] : v[j + m];
-                    const float keep = up ? v[j + m] : v[j];
-                    v[j] = keep + __shfl_xor_sync(FULL, send, m * 4);
+                    for (int v = 0; v < 4; ++v) {
+                        const float send = up ? sv[r][v] : sv[r + 2][v];
+                        const float keep = up ? sv[r + 2][v] : sv[r][v];
+                        sv[r][v] = keep + __shfl_xor_sync(FULL, send, 2);
+                    }
+            }
+            {
+                const bool up = (sg & 1) != 0;
+#pragma unroll
+                for (int v = 0; v < 4; ++v) {
+                    const float send = up ? sv[0][v] : sv[1][v];
+                    const float keep = up ? sv[1][v] : sv[0][v];
+                    sv[0][v] = keep + __shfl_xor_sync(FULL, send, 1);
                 }
             }
-            s.red[rb][w][i][oidx] = v[0];
-            if (sg == 0) {
-                const float du0 = fmaf(gy[0], Dd[0], dt[0] * S2[0]);
-                const float du1 = fmaf(gy[1], Dd[1], dt[1] * S2[1]);
-                const float dd0 = fmaf(uu[0], S2[0], S1[0] * LN2);
-                const float dd1 = fmaf(uu[1], S2[1], S1[1] * LN2);
+            {
+                const int i = i0 + sg;
+                float dq[2], uq[2], gq[2];
+                load2<T>(dq, &s.d[st][i][c2]);
+                load2<T>(uq, &s.u[st][i][c2]);
+                load2<T>(gq, &s.g[st][i][c2]);
+                const float du0 = fmaf(gq[0], Dd[0], dq[0] * sv[0][2]);
+                const float du1 = fmaf(gq[1], Dd[1], dq[1] * sv[0][3]);
+                const float dd0 = fmaf(uq[0], sv[0][2], sv[0][0] * LN2);
+                const float dd1 = fmaf(uq[1], sv[0][3], sv[0][1] * LN2);
                 if constexpr (Cfg::STAGE_OUT) {
                     store2<T>(&s.duo[ob][i][c2], du0, du1);
                     store2<T>(&s.ddo[ob][i][c2], dd0, dd1);
@@ -551,11 +560,39 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                     }
                 }
             }
+            // dB | dC over the warp's 8 channel pairs: reduce-scatter (xor 16, 8, 4); lane
+            // (cg, sg) ends with step i0 + cg / 2, part cg % 2 (dB, dC), states 4sg..4sg+3
+            {
+                const bool up = (cg & 4) != 0;
 #pragma unroll
-            for (int cc = 0; cc < 2; ++cc) {
-                ht[cc][0] = hp[cc][0];
-                ht[cc][1] = hp[cc][1];
+                for (int r = 0; r < 2; ++r)
+#pragma unroll
+                    for (int k2 = 0; k2 < 8; ++k2) {
+                        const float send = up ? vv[r][k2] : vv[r + 2][k2];
+                        const float keep = up ? vv[r + 2][k2] : vv[r][k2];
+                        vv[r][k2] = keep + __shfl_xor_sync(FULL, send, 16);
+                    }
             }
+            {
+                const bool up = (cg & 2) != 0;
+#pragma unroll
+                for (int k2 = 0; k2 < 8; ++k2) {
+                    const float send = up ? vv[0][k2] : vv[1][k2];
+                    const float keep = up ? vv[1][k2] : vv[0][k2];
+                    vv[0][k2] = keep + __shfl_xor_sync(FULL, send, 8);
+                }
+            }
+            {
+                const bool up = (cg & 1) != 0;
+#pragma unroll
+                for (int k2 = 0; k2 < 4; ++k2) {
+                    const float send = up ? vv[0][k2] : vv[0][k2 + 4];
+                    const float keep = up ? vv[0][k2 + 4] : vv[0][k2];
+                    vv[0][k2] = keep + __shfl_xor_sync(FULL, send, 4);
+                }
+            }
+            *reinterpret_cast<float4*>(&s.red[rb][w][i0 + (cg >> 1)][(cg & 1) * NSTATE + 4 * sg]) =
+                make_float4(vv[0][0], vv[0][1], vv[0][2], vv[0][3]);
         }
         // inputs of the stage consumed; partials and output tile written
         __syncwarp();
