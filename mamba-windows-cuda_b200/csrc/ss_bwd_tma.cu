@@ -38,7 +38,11 @@ constexpr int PB_CPB = 128;
 constexpr int PB_NCW = 8;                    // compute warps
 constexpr int PB_NCT = PB_NCW * 32;          // compute threads
 constexpr int PB_NT = (PB_NCW + 2) * 32;     // + producer warp + helper warp
-constexpr int PB_ST = 2;
+constexpr int PB_ST = 4;
+// TMEM state cache: per compute thread and step, the state before the step (8 values) and
+// the decay factors of the step (8 values); 16 steps x 16 columns = 256 columns per thread,
+// warps w and w + 4 share a lane quarter and split the 512 columns.
+constexpr uint32_t PB_TMEM_COLS = 512;
 #ifndef MWC_BWD_MIN_SEG_TILES
 #define MWC_BWD_MIN_SEG_TILES 4   // shortest segment (in 16-step tiles) the planner may pick
 #endif
@@ -53,8 +57,10 @@ struct PbCfg {
 template <typename T>
 struct __align__(128) PBwdSmem {
     using C = PbCfg<T>;
-    float4 hc[PB_LT][2][PB_NCT];                 // state cache: [step][channel c][thread]
     float h0[PB_ST][PB_CPB][NSTATE];             // checkpoint at the chunk start
+    float qin[PB_ST][PB_CPB][NSTATE];            // incoming adjoint state (unit start)
+    T At[PB_ST][PB_CPB][NSTATE];                 // unit parameters: A rows,
+    T Dt[PB_ST][PB_CPB];                         // D
     T u[PB_ST][PB_LT][PB_CPB];
     T d[PB_ST][PB_LT][PB_CPB];
     T g[PB_ST][PB_LT][PB_CPB];
@@ -65,10 +71,11 @@ struct __align__(128) PBwdSmem {
     float red[C::RB][PB_NCW][PB_LT][2 * NSTATE];  // per-warp dB | dC partials of a tile
     float Bf[C::HALF ? PB_ST : 1][PB_LT][NSTATE];
     float Cf[C::HALF ? PB_ST : 1][PB_LT][NSTATE];
-    uint64_t full[PB_ST], conv[PB_ST], empty[PB_ST];
+    uint64_t full[PB_ST], conv[PB_ST], empty[PB_ST], qfull[PB_ST];
     uint64_t redfull[C::RB], redempty[C::RB], ofull[2], oempty[2];
     int unit[PB_ST];
     int tile[PB_ST];
+    uint32_t tmem_base;
 };
 
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
@@ -161,6 +168,7 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
             mbar_init(&s.full[i], 1);
             mbar_init(&s.conv[i], 1);
             mbar_init(&s.empty[i], PB_NCW);
+            mbar_init(&s.qfull[i], 1);
         }
         for (int i = 0; i < RB; ++i) {
             mbar_init(&s.redfull[i], PB_NCW);
@@ -172,7 +180,13 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
         }
         fence_mbar_init();
     }
+    if (w == 0) {   // one CTA per SM (shared memory > half the SM), so the allocation succeeds
+        tmem_alloc(&s.tmem_base, PB_TMEM_COLS);
+        tmem_relinquish();
+    }
+    tmem_fence_before_sync();
     __syncthreads();
+    tmem_fence_after_sync();
 
     if (w == PB_NCW) {
         // ============================== producer ==============================
@@ -205,12 +219,10 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
             const int t0 = tix * PB_LT;
             s.unit[st] = pu;
             s.tile[st] = pcount;
-            // the successor segment's adjoint state must be published before the unit's
-            // compute warps read it (they read it after this stage's barrier completes)
-            if (pcount == 0 && kp > 0) flag_wait(&p.flags[c * p.K + kp - 1], PB_NCW, p.err);
             const int nch = min(PB_CPB, p.D - blk * PB_CPB);
             const unsigned hbytes = tix > 0 ? (unsigned)(nch * NSTATE * 4) : 0u;
-            mbar_expect_tx(&s.full[st], tile_bytes + hbytes);
+            const unsigned rbytes = pcount == 0 ? (unsigned)(nch * (NSTATE + 1) * sizeof(T)) : 0u;
+            mbar_expect_tx(&s.full[st], tile_bytes + hbytes + rbytes);
             tma_load_3d(&s.u[st][0][0], &p.tm_u, &s.full[st], blk * PB_CPB, t0, b);
             tma_load_3d(&s.d[st][0][0], &p.tm_d, &s.full[st], blk * PB_CPB, t0, b);
             tma_load_3d(&s.g[st][0][0], &p.tm_g, &s.full[st], blk * PB_CPB, t0, b);
@@ -220,6 +232,22 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                 bulk_load(&s.h0[st][0][0],
                           p.ckpt + (((int64_t)b * p.nck + tix - 1) * p.D + (int64_t)blk * PB_CPB) * NSTATE,
                           hbytes, &s.full[st]);
+            if (pcount == 0) {
+                bulk_load(&s.At[st][0][0], static_cast<const T*>(p.A) + (int64_t)blk * PB_CPB * NSTATE,
+                          (unsigned)(nch * NSTATE * sizeof(T)), &s.full[st]);
+                bulk_load(&s.Dt[st][0], static_cast<const T*>(p.Dv) + (int64_t)blk * PB_CPB,
+                          (unsigned)(nch * sizeof(T)), &s.full[st]);
+                if (kp > 0) {
+                    // the tile is already on its way; the adjoint state of the successor
+                    // segment follows on its own barrier, which the compute warps wait for
+                    // only after their recompute pass
+                    flag_wait(&p.flags[c * p.K + kp - 1], PB_NCW, p.err);
+                    fence_proxy_async_global();
+                    mbar_expect_tx(&s.qfull[st], (unsigned)(PB_CPB * NSTATE * 4));
+                    bulk_load(&s.qin[st][0][0], p.hand + (int64_t)(c * p.K + kp - 1) * PB_CPB * NSTATE,
+                              (unsigned)(PB_CPB * NSTATE * 4), &s.qfull[st]);
+                }
+            }
             ++pcount;
         }
     }
@@ -291,13 +319,13 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
 
     // ================================ compute warps ================================
     const int cg = lane >> 2, sg = lane & 3;
+    const uint32_t tcache = s.tmem_base + ((uint32_t)(32 * (w & 3)) << 16) + (uint32_t)(w >> 2) * 256u;
     const int c2 = w * 16 + cg * 2;          // first of the thread's 2 channels in the block
-    const T* Ap = static_cast<const T*>(p.A);
-    const T* Dp = static_cast<const T*>(p.Dv);
     float2 A2[2][2], q[2][2], dA[2][2];
     float Dd[2], dD[2];
     bool a_nonpos = true;   // warp-uniform: A <= 0, so delta >= 0 keeps every exponent <= 0
     int64_t dbase = 0;
+    unsigned qphase = 0;    // bit st: parity of the next wait on qfull[st]
 
     for (int it = 0;; ++it) {
         const int st = it % PB_ST;
@@ -323,10 +351,10 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
 #pragma unroll
             for (int cc = 0; cc < 2; ++cc) {
                 float a4[4] = {0.f, 0.f, 0.f, 0.f};
-                if (dvc[cc]) load4<T>(a4, Ap + (dbase + cc) * NSTATE + 4 * sg);
+                if (dvc[cc]) load4<T>(a4, &s.At[st][c2 + cc][4 * sg]);
                 A2[cc][0] = make_float2(a4[0] * LOG2E, a4[1] * LOG2E);
                 A2[cc][1] = make_float2(a4[2] * LOG2E, a4[3] * LOG2E);
-                Dd[cc] = dvc[cc] ? to_f(Dp[dbase + cc]) : 0.f;
+                Dd[cc] = dvc[cc] ? to_f(s.Dt[st][c2 + cc]) : 0.f;
                 dD[cc] = 0.f;
                 dA[cc][0] = dA[cc][1] = make_float2(0.f, 0.f);
             }
@@ -342,15 +370,8 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                     q[cc][0] = make_float2(g4[0], g4[1]);
                     q[cc][1] = make_float2(g4[2], g4[3]);
                 }
-            } else {
-                const float* hs = p.hand + ((int64_t)(c * p.K + kp - 1) * PB_CPB + c2) * NSTATE + 4 * sg;
-#pragma unroll
-                for (int cc = 0; cc < 2; ++cc) {
-                    const float4 v = __ldcg(reinterpret_cast<const float4*>(hs + cc * NSTATE));
-                    q[cc][0] = make_float2(v.x, v.y);
-                    q[cc][1] = make_float2(v.z, v.w);
-                }
             }
+            // otherwise q arrives on qfull[st], read before the adjoint pass
         }
 
         const float* Bf = HALF ? &s.Bf[HALF ? st : 0][0][0] : reinterpret_cast<const float*>(&s.Bt[st][0][0]);
@@ -374,8 +395,9 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
             h[cc][1] = make_float2(v.z, v.w);
         }
 
-        // ---- recompute: hc[i] = state before step i; h ends as the state after the last
-        //      step (blocks of 4 steps: loads, then the serial updates) ----
+        // ---- recompute: TMEM column block i = (state before step i, decay factors of step i);
+        //      h ends as the state after the last step (blocks of 4 steps: loads, then the
+        //      serial updates) ----
 #pragma unroll 1
         for (int i0 = 0; i0 < PB_LT; i0 += 4) {
             float dt[4][2], uu[4][2];
@@ -412,15 +434,37 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
                 const float2 Bp0 = make_float2(B4[r].x, B4[r].y), Bp1 = make_float2(B4[r].z, B4[r].w);
+                uint32_t tv[16];
 #pragma unroll
                 for (int cc = 0; cc < 2; ++cc) {
-                    s.hc[i0 + r][cc][tid] = make_float4(h[cc][0].x, h[cc][0].y, h[cc][1].x, h[cc][1].y);
                     const float2 du2 = f2(dt[r][cc] * uu[r][cc]);
                     const float2 a0 = make_float2(ex2(x[r][cc][0].x), ex2(x[r][cc][0].y));
                     const float2 a1 = make_float2(ex2(x[r][cc][1].x), ex2(x[r][cc][1].y));
+                    tv[4 * cc + 0] = __float_as_uint(h[cc][0].x);
+                    tv[4 * cc + 1] = __float_as_uint(h[cc][0].y);
+                    tv[4 * cc + 2] = __float_as_uint(h[cc][1].x);
+                    tv[4 * cc + 3] = __float_as_uint(h[cc][1].y);
+                    tv[8 + 4 * cc + 0] = __float_as_uint(a0.x);
+                    tv[8 + 4 * cc + 1] = __float_as_uint(a0.y);
+                    tv[8 + 4 * cc + 2] = __float_as_uint(a1.x);
+                    tv[8 + 4 * cc + 3] = __float_as_uint(a1.y);
                     h[cc][0] = __ffma2_rn(a0, h[cc][0], __fmul2_rn(du2, Bp0));
                     h[cc][1] = __ffma2_rn(a1, h[cc][1], __fmul2_rn(du2, Bp1));
                 }
+                tmem_st16(tcache + (uint32_t)(i0 + r) * 16u, tv);
+            }
+        }
+        tmem_wait_st();   // the adjoint pass reads these columns back
+
+        if (pc == 0 && kp > 0) {
+            mbar_wait(&s.qfull[st], (qphase >> st) & 1u, p.err);
+            qphase ^= 1u << st;
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) {
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (dvc[cc]) v = *reinterpret_cast<const float4*>(&s.qin[st][c2 + cc][4 * sg]);
+                q[cc][0] = make_float2(v.x, v.y);
+                q[cc][1] = make_float2(v.z, v.w);
             }
         }
 
@@ -447,10 +491,11 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                 load2<T>(uu[r], &s.u[st][i0 + r][c2]);
                 load2<T>(gy[r], &s.g[st][i0 + r][c2]);
             }
-            float dmin = INFINITY;
+            uint32_t tv[4][16];   // per step: state before the step, then its decay factors
 #pragma unroll
-            for (int r = 0; r < 4; ++r) dmin = fminf(dmin, fminf(dt[r][0], dt[r][1]));
-            const bool fast = a_nonpos && __all_sync(FULL, dmin >= 0.f);
+            for (int r = 0; r < 4; ++r) tmem_ld16(tcache + (uint32_t)(i0 + r) * 16u, tv[r]);
+#pragma unroll
+            for (int r = 0; r < 4; ++r) tmem_wait_ld(tv[r]);
             float vv[4][8];   // per step: dB partial (states 4sg..4sg+3), then dC partial
             float sv[4][4];   // per step: S1 (channels c2, c2+1), then S2
 #pragma unroll
@@ -460,26 +505,16 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                 const float4 C4 = *reinterpret_cast<const float4*>(Cf + i * NSTATE + 4 * sg);
                 const float2 Bp[2] = {make_float2(B4.x, B4.y), make_float2(B4.z, B4.w)};
                 const float2 Cp[2] = {make_float2(C4.x, C4.y), make_float2(C4.z, C4.w)};
-                float2 hp[2][2];   // state before step i
+                float2 hp[2][2], av[2][2];   // state before step i, decay factors of step i
 #pragma unroll
-                for (int cc = 0; cc < 2; ++cc) {
-                    const float4 v = s.hc[i][cc][tid];
-                    hp[cc][0] = make_float2(v.x, v.y);
-                    hp[cc][1] = make_float2(v.z, v.w);
-                }
-                float2 x[2][2];
+                for (int cc = 0; cc < 2; ++cc)
 #pragma unroll
-                for (int cc = 0; cc < 2; ++cc) {
-                    x[cc][0] = __fmul2_rn(f2(dt[r][cc]), A2[cc][0]);
-                    x[cc][1] = __fmul2_rn(f2(dt[r][cc]), A2[cc][1]);
-                }
-                if (!fast) {
-#pragma unroll
-                    for (int cc = 0; cc < 2; ++cc)
-#pragma unroll
-                        for (int pr = 0; pr < 2; ++pr)
-                            x[cc][pr] = make_float2(fminf(x[cc][pr].x, ARG2_HI), fminf(x[cc][pr].y, ARG2_HI));
-                }
+                    for (int pr = 0; pr < 2; ++pr) {
+                        hp[cc][pr] = make_float2(__uint_as_float(tv[r][4 * cc + 2 * pr]),
+                                                 __uint_as_float(tv[r][4 * cc + 2 * pr + 1]));
+                        av[cc][pr] = make_float2(__uint_as_float(tv[r][8 + 4 * cc + 2 * pr]),
+                                                 __uint_as_float(tv[r][8 + 4 * cc + 2 * pr + 1]));
+                    }
                 float2 vB[2], vC[2];
 #pragma unroll
                 for (int cc = 0; cc < 2; ++cc) {
@@ -489,7 +524,7 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                     float2 s1, s2;
 #pragma unroll
                     for (int pr = 0; pr < 2; ++pr) {
-                        const float2 a = make_float2(ex2(x[cc][pr].x), ex2(x[cc][pr].y));
+                        const float2 a = av[cc][pr];
                         const float2 g = __ffma2_rn(gy2, Cp[pr], q[cc][pr]);
                         const float2 pp = __fmul2_rn(g, __fmul2_rn(a, hp[cc][pr]));
                         s1 = pr == 0 ? __fmul2_rn(A2[cc][pr], pp) : __ffma2_rn(A2[cc][pr], pp, s1);
@@ -632,6 +667,14 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
             }
         }
     }
+    // every compute warp leaves the loop on the same (terminating) stage; then warp 0 frees
+    // the TMEM columns
+    tmem_fence_before_sync();
+    asm volatile("bar.sync 1, %0;" ::"n"(PB_NCT) : "memory");
+    if (w == 0) {
+        tmem_fence_after_sync();
+        tmem_dealloc(s.tmem_base, PB_TMEM_COLS);
+    }
 }
 
 // Fixed-order sums of the persistent backward's partials into dA, dD (over batch rows and
@@ -717,10 +760,15 @@ BwdPersistWs bwd_persistent_ws(const PersistPlan& pl, int64_t B, int64_t L) {
     return w;
 }
 
+static_assert(sizeof(PBwdSmem<float>) <= 227 * 1024 && sizeof(PBwdSmem<__half>) <= 227 * 1024,
+              "backward shared memory exceeds the 227 KB a CTA may use");
+
 template <typename T>
 static cudaError_t launch_pb(const PBwdArgs& a, int grid, void* dA, void* dB, void* dC, void* dD,
                              cudaStream_t s) {
-    const size_t smem = sizeof(PBwdSmem<T>);
+    // more than half of the SM's shared memory: one CTA per SM, so the CTA's 512-column TMEM
+    // allocation never waits for another CTA of this kernel
+    const size_t smem = std::max(sizeof(PBwdSmem<T>), (size_t)(120 * 1024));
     cudaError_t e = cudaFuncSetAttribute(ss_bwd_persistent_kernel<T>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
