@@ -52,6 +52,15 @@ CONFIGS = {
 }
 
 
+# DRAM bytes (read + write) of one launch of the dominant kernel, from one ncu capture of
+# this bench's own command (profiles/ss_fwd_bwd_persistent_c3_fp16.md).
+CAPTURED_TRAFFIC = {
+    "c3": {"bytes": 419.062784e6 + 205.661440e6,
+           "source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, ss_bwd_persistent_kernel, "
+                     "profiles/ss_fwd_bwd_persistent_c3_fp16.md"},
+}
+
+
 def load_peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -325,10 +334,13 @@ def bench_fwdbwd(args, cfg, dev, world, rank, peaks):
     rb = roof(bwd_bytes, 16 * E, bwd_ms)
     rf = roof(fwd_bytes, 16 * E, fwd_ms)
     rs = roof(nbytes, 32 * E, ms / args.steps)
+    traffic = CAPTURED_TRAFFIC.get(args.config)
     roofline = {
-        "kernel": "ss_bwd_kernel + ss_bwd_final_kernel (backward op)",
+        "kernel": "ss_bwd_persistent_kernel + ss_bwd_persistent_final_kernel (backward op)",
         "bound": "mufu", "achieved": rb["ex2_per_s"] / 1e9, "peak": mufu_peak / 1e9,
-        "unit": "Gex2/s", "frac": rb["mufu_frac"], "traffic": None,
+        "unit": "Gex2/s", "frac": rb["mufu_frac"],
+        "traffic": traffic["bytes"] if traffic else None,
+        "traffic_source": traffic["source"] if traffic else None,
         "hbm": {"achieved": rb["hbm_gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": rb["hbm_frac"], "peak_source": peaks["source"]},
         "model": "max(algorithmic bytes / HBM, 16 ex2 per element / MUFU at 148 SM x 16/clk x sm_max_mhz)",

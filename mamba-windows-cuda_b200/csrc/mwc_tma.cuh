@@ -12,7 +12,15 @@ namespace mwc {
 constexpr int ERR_WAIT_TMA = 1;     // a TMA tile never arrived
 constexpr int ERR_WAIT_CHAIN = 2;   // the previous segment of a chain never published its state
 constexpr int ERR_SMEM_ALIGN = 3;   // dynamic shared memory not 128-byte aligned (kernel exits)
-constexpr unsigned WAIT_SPINS = 1u << 24;   // a few seconds with the backoff below
+constexpr unsigned WAIT_SPINS = 1u << 22;   // per wait: a fraction of a second with the backoff
+constexpr unsigned WAIT_POLL = 1024;        // a waiting thread reads the error word this often
+
+// True once any wait of the launch has given up: the protocol is broken, so every other
+// wait returns at once instead of running to its own limit (the kernel then drains its
+// loops quickly and exits normally, releasing what it holds).
+__device__ __forceinline__ bool wait_aborted(const int* err) {
+    return err != nullptr && *reinterpret_cast<const volatile int*>(err) != 0;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -49,6 +57,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned phase, int* er
     for (unsigned it = 0; it < WAIT_SPINS; ++it) {
         if (mbar_try_wait(bar, phase)) return true;
         if (it > 64) __nanosleep(32);
+        if ((it & (WAIT_POLL - 1)) == WAIT_POLL - 1 && wait_aborted(err)) return false;
     }
     if (err) atomicCAS(err, 0, ERR_WAIT_TMA);
     return false;
@@ -106,6 +115,7 @@ __device__ __forceinline__ bool flag_wait(const int* f, int v, int* err) {
     for (unsigned it = 0; it < WAIT_SPINS; ++it) {
         if (flag_acquire(f) == v) return true;
         __nanosleep(it < 64 ? 20 : 200);
+        if ((it & (WAIT_POLL - 1)) == WAIT_POLL - 1 && wait_aborted(err)) return false;
     }
     if (err) atomicCAS(err, 0, ERR_WAIT_CHAIN);
     return false;

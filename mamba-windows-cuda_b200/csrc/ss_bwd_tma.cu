@@ -181,6 +181,7 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
         fence_mbar_init();
     }
     if (w == 0) {   // one CTA per SM (shared memory > half the SM), so the allocation succeeds
+        __syncwarp();   // lane 0 initialised the barriers; the allocation is warp-collective
         tmem_alloc(&s.tmem_base, PB_TMEM_COLS);
         tmem_relinquish();
     }
@@ -374,6 +375,9 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
             // otherwise q arrives on qfull[st], read before the adjoint pass
         }
 
+        // tcgen05 loads / stores are warp-collective (.sync.aligned): reconverge the lanes,
+        // which leave the barrier spin loops and the divergent unit-boundary code separately
+        __syncwarp();
         const float* Bf = HALF ? &s.Bf[HALF ? st : 0][0][0] : reinterpret_cast<const float*>(&s.Bt[st][0][0]);
         const float* Cf = HALF ? &s.Cf[HALF ? st : 0][0][0] : reinterpret_cast<const float*>(&s.Ct[st][0][0]);
 
@@ -398,6 +402,7 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
         // ---- recompute: TMEM column block i = (state before step i, decay factors of step i);
         //      h ends as the state after the last step (blocks of 4 steps: loads, then the
         //      serial updates) ----
+        __syncwarp();   // the chunk-start loads above depend on the channel's lane
 #pragma unroll 1
         for (int i0 = 0; i0 < PB_LT; i0 += 4) {
             float dt[4][2], uu[4][2];
@@ -476,6 +481,7 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
         if constexpr (Cfg::STAGE_OUT) mbar_wait(&s.oempty[ob], ((unsigned)(it / 2) & 1u) ^ 1u, p.err);
         T* dub = static_cast<T*>(p.du);
         T* ddb = static_cast<T*>(p.ddelta);
+        __syncwarp();
         float2 ht[2][2];   // state after the step being processed
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
@@ -492,6 +498,7 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                 load2<T>(gy[r], &s.g[st][i0 + r][c2]);
             }
             uint32_t tv[4][16];   // per step: state before the step, then its decay factors
+            __syncwarp();         // the output stores of the previous block may diverge
 #pragma unroll
             for (int r = 0; r < 4; ++r) tmem_ld16(tcache + (uint32_t)(i0 + r) * 16u, tv[r]);
 #pragma unroll
@@ -668,7 +675,8 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
         }
     }
     // every compute warp leaves the loop on the same (terminating) stage; then warp 0 frees
-    // the TMEM columns
+    // the TMEM columns (warp-collective: reconverge first)
+    __syncwarp();
     tmem_fence_before_sync();
     asm volatile("bar.sync 1, %0;" ::"n"(PB_NCT) : "memory");
     if (w == 0) {
