@@ -45,8 +45,10 @@ CONFIGS = {
                B=1, L=1024, D=256, dtype=torch.float32, mode="fwdbwd", dist="c1"),
     "c2": dict(workload="config 2: Mamba-1.4B-like inference forward_with_state fp16",
                B=8, L=2048, D=4096, dtype=torch.float16, mode="fwd", dist="c2"),
-    "c4": dict(workload="config 4: streaming scan fp32, 16 chunks of 65536 with h_prev/h_last",
-               B=1, L=65536, D=2048, dtype=torch.float32, mode="stream", dist="c4", chunks=16),
+    "c4": dict(workload="config 4: streaming scan fp32, 16 chunks of 65536 with h_prev/h_last "
+                        "(2^20 tokens; sequence-sharded across ranks for N > 1)",
+               B=1, L=65536, D=2048, dtype=torch.float32, mode="stream", dist="c4", chunks=16,
+               metric="selective-scan streaming forward GB/s, B=1 L=2^20 (16 x 65536) D=2048 fp32"),
     "c5": dict(workload="config 5: parallel_scan_fn fp32 (16, 1024, 16384, 1)",
                B=16, L=16384, D=1024, dtype=torch.float32, mode="pscan", dist="c5"),
 }
@@ -263,9 +265,11 @@ def reference_arm(args, cfg):
     tot_b = sum(b for _, b in times)
     gbs = tot_b / tot_s / 1e9
     line = {
-        "impl": "reference", "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": args.gpus,
+        "impl": "reference", "metric": cfg.get("metric", METRIC), "value": gbs, "unit": "GB/s",
+        "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * tot_s / len(times),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "higher_is_better": True, "scaling": "strong" if cfg["mode"] == "stream" else "weak",
+        "vs_baseline": None, "dtype": "f64",
         "data": "synthetic (seeded, BASELINE distributions)",
         "config": {"workload": cfg["workload"], "B": cfg["B"], "L": cfg["L"], "D": cfg["D"],
                    "N": NSTATE, "sample_per_step": desc},
@@ -381,6 +385,88 @@ def bench_fwdbwd(args, cfg, dev, world, rank, peaks):
                 dtype="f32", io_dtype=str(cfg["dtype"]).replace("torch.", ""))
 
 
+def bench_stream(args, cfg, dev, world, rank, peaks):
+    """Config 4: forward over a 2^20-token sequence (16 chunks of 65536), B=1, D=2048, fp32.
+
+    N=1: the chunks run in order through ``SelectiveScanCuda.forward_with_state`` (h_prev ->
+    h_last), the reference's streaming use. N>1: sequence sharding (strong scaling, the
+    sequence is fixed): rank r owns chunks split_range(16, N, r) as one contiguous range and
+    runs ``sharding.sequence_sharded_forward`` (local scan from zero, NCCL all-gather of the
+    float32 (decay, end state) pairs, carry fold, ``mwc_ss_fixup``)."""
+    import mamba_windows_cuda as mwc
+    from mamba_windows_cuda import sharding as S
+    B, Lc, D, nch = cfg["B"], cfg["L"], cfg["D"], cfg["chunks"]
+    c0, c1 = S.split_range(nch, world, rank)
+    Lr = (c1 - c0) * Lc
+    ins, _ = make_ss_inputs(cfg, dev, seed=3000 + rank, L=Lr)
+    u, delta, A, Bm, Cm, Dv = ins
+    es = u.element_size()
+    h0 = torch.zeros(B, D, NSTATE, dtype=cfg["dtype"], device=dev) if rank == 0 else None
+    mod = mwc.SelectiveScanCuda()
+    stream = torch.cuda.current_stream(dev)
+    lib = mwc._lib.load()
+    dcode = 1 if es == 2 else 0
+
+    if world == 1:
+        def step():
+            h = h0
+            with torch.no_grad():
+                for c in range(nch):
+                    sl = slice(c * Lc, (c + 1) * Lc)
+                    _, h = mod.forward_with_state(u[:, sl], delta[:, sl], A, Bm[:, sl], Cm[:, sl], Dv, h)
+            return h
+        per_call = 1 if int(lib.mwc_ss_fwd_workspace_bytes(B, Lc, D, dcode)) == 0 else 2
+        launches = nch * per_call
+    else:
+        def step():
+            with torch.no_grad():
+                _, h = S.sequence_sharded_forward(u, delta, A, Bm, Cm, Dv, h0)
+            return h
+        per_call = 1 if int(lib.mwc_ss_fwd_workspace_bytes(B, Lr, D, dcode)) == 0 else 2
+        launches = per_call + (1 if rank > 0 else 0)
+
+    for _ in range(args.warmup):
+        step()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier_sync(world, dev)
+    with ClockSampler(dev.index if dev.index is not None else 0) as clk:
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        stop.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier_sync(world, dev)
+    ms = start.elapsed_time(stop)
+    ms_max = max_over_ranks(ms, world, dev)
+    Ltot = Lc * nch
+    nbytes = ss_bytes(B, Ltot, D, es, "stream")
+    value = nbytes / (ms_max / args.steps / 1e3) / 1e9
+    mufu_peak = 148 * 16 * peaks["sm_max_mhz"] * 1e6
+    t_rank = ms / args.steps / 1e3
+    ex2_rank = 16 * B * Lr * D
+    bytes_rank = ss_bytes(B, Lr, D, es, "stream")
+    roofline = {
+        "kernel": "forward scan of this rank's range (ss_fwd_kernel + ss_fixup_kernel, L-segmented)",
+        "bound": "mufu", "achieved": ex2_rank / t_rank / 1e9, "peak": mufu_peak / 1e9,
+        "unit": "Gex2/s", "frac": ex2_rank / t_rank / mufu_peak, "traffic": None,
+        "hbm": {"achieved": bytes_rank / t_rank / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": bytes_rank / t_rank / 1e9 / peaks["hbm_gbs"], "peak_source": peaks["source"]},
+        "model": "per rank: 16 ex2 per element of its range / MUFU; step time includes the "
+                 "carry exchange and fixup for N > 1",
+    }
+    e2e = {"value": None, "unit": "GB/s", "h2d_bytes_per_step": None, "d2h_bytes_per_step": None,
+           "note": "not measured for config 4: its 25.8 GB of fp32 inputs per step are "
+                   "generated on the device; the host-buffer e2e line is config 3's"}
+    return dict(value=value, ms_per_step=ms_max / args.steps, roofline=roofline, e2e=e2e,
+                clocks=clk.summary(), gpu_launches=launches * args.steps, dtype="f32",
+                io_dtype=str(cfg["dtype"]).replace("torch.", ""), scaling="strong",
+                parallelism=(f"sequence-sharded x{world}: chunks {c0}..{c1 - 1} on rank {rank}, "
+                             "NCCL all-gather of (decay, end state) + carry fixup")
+                if world > 1 else "single GPU, 16 chunks chained through h_prev / h_last",
+                l2=f"{3 * B * Lr * D * es / 1e9:.1f} GB of u / delta / y per rank per step, "
+                   "far above the 126 MB L2; no flush")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -405,20 +491,25 @@ def main():
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    if cfg["mode"] != "fwdbwd":
-        raise SystemExit(f"--config {args.config}: use the per-config scripts in the tests; "
-                         "bench.py measures the fwd+bwd workloads")
-    res = bench_fwdbwd(args, cfg, dev, world, rank, peaks)
+    if cfg["mode"] == "stream":
+        res = bench_stream(args, cfg, dev, world, rank, peaks)
+    elif cfg["mode"] == "fwdbwd":
+        res = bench_fwdbwd(args, cfg, dev, world, rank, peaks)
+    else:
+        raise SystemExit(f"--config {args.config}: mode {cfg['mode']} is covered by the tests; "
+                         "bench.py measures the fwd+bwd (c1, c3) and streaming (c4) workloads")
 
     line = {
-        "metric": METRIC, "value": res["value"], "unit": "GB/s", "n_gpus": world,
+        "metric": cfg.get("metric", METRIC), "value": res["value"], "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": res.get("scaling", "weak"), "vs_baseline": None,
         "dtype": res["dtype"], "data": "synthetic (seeded, BASELINE distributions, generated on device)",
         "config": {"workload": cfg["workload"], "B": cfg["B"], "L": cfg["L"], "D": cfg["D"],
                    "N": NSTATE, "io_dtype": res["io_dtype"],
-                   "l2": "inputs + outputs per step (~250 MB at config 3) exceed the 126 MB L2; no flush",
-                   "parallelism": f"replicas x{world}: one independent batch per rank, no collective"},
+                   "l2": res.get("l2", "inputs + outputs per step (~250 MB at config 3) exceed the "
+                                       "126 MB L2; no flush"),
+                   "parallelism": res.get("parallelism", f"replicas x{world}: one independent "
+                                                         "batch per rank, no collective")},
         "roofline": res["roofline"], "e2e": res["e2e"], "gpu_launches": res["gpu_launches"],
         "clocks": res["clocks"],
     }

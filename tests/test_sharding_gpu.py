@@ -1,0 +1,99 @@
+"""GPU tests of sequence sharding through the CUDA entry points (local scans with the
+segment decay, carry fold, mwc_ss_fixup), against the single-call CUDA scan of the whole
+sequence and the float64 oracle. Ranks are emulated in one process on one GPU; the NCCL
+test with one process per GPU runs when two or more GPUs are visible."""
+from __future__ import annotations
+
+import os
+import socket
+import tempfile
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from _helpers import assert_fp16, assert_fp32, make_inputs, np64
+from mamba_windows_cuda import _ops
+from mamba_windows_cuda import sharding as S
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _need_gpu(n=1):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < n:
+        pytest.skip(f"needs {n} CUDA GPU(s)")
+
+
+CASES = [
+    # (dtype, B, L, D, world, dist)
+    (torch.float32, 1, 8192, 256, 4, "c4"),
+    (torch.float32, 1, 8192, 256, 8, "c4"),
+    (torch.float32, 2, 3000, 96, 3, "c1"),      # ragged ranges, strong decay
+    (torch.float16, 1, 8192, 256, 8, "c4"),
+    (torch.float32, 1, 65536, 2048, 8, "c4"),   # config-4 chunk spread over 8 ranks
+]
+
+
+@pytest.mark.parametrize("dtype,B,L,D,world,dist", CASES)
+def test_emulated_sequence_sharding(dtype, B, L, D, world, dist):
+    _need_gpu()
+    x = make_inputs(B, L, D, dtype, seed=21, dist=dist, with_state=True, device="cuda")
+    args = [x[k] for k in ("u", "delta", "A", "Bm", "Cm", "Dv")]
+    out, h_last = S.emulated_sequence_sharded_forward(*args, x["h_prev"], world=world)
+    ref_out, ref_h, _, _ = _ops.ss_forward(*args, x["h_prev"], want_h_last=True)
+    torch.cuda.synchronize()
+    if dtype == torch.float32:
+        assert_fp32(out, ref_out.double().cpu().numpy(), what="out vs single-call scan")
+        assert_fp32(h_last, ref_h.double().cpu().numpy(), what="h_last vs single-call scan")
+        if L * D <= 8192 * 256:
+            o64, h64 = O.ss_fwd(*[np64(t) for t in args], np64(x["h_prev"]))
+            assert_fp32(out, o64, what="out vs oracle")
+            assert_fp32(h_last, h64, what="h_last vs oracle")
+    else:
+        o64, h64 = O.ss_fwd(*[np64(t) for t in args], np64(x["h_prev"]))
+        assert_fp16(out, o64, what="out vs oracle")
+        assert_fp16(h_last, h64, what="h_last vs oracle")
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _nccl_worker(rank, world, port, outdir):
+    import datetime
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        x = make_inputs(1, 16384, 512, torch.float32, seed=31, dist="c4", with_state=True,
+                        device=f"cuda:{rank}")
+        args = [x[k] for k in ("u", "delta", "A", "Bm", "Cm", "Dv")]
+        a, b = S.split_range(x["u"].shape[1], world, rank)
+        part = [t[:, a:b].contiguous() if t.dim() == 3 else t for t in args]
+        out, h_last = S.sequence_sharded_forward(*part, x["h_prev"], broadcast_h_last=True)
+        torch.cuda.synchronize()
+        np.save(os.path.join(outdir, f"out{rank}.npy"), out.double().cpu().numpy())
+        np.save(os.path.join(outdir, f"h{rank}.npy"), h_last.double().cpu().numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_nccl_sequence_sharding_two_ranks():
+    _need_gpu(2)
+    world = 2
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_nccl_worker, args=(world, _free_port(), d), nprocs=world,
+                           start_method="spawn", join=True)
+        out = np.concatenate([np.load(os.path.join(d, f"out{r}.npy")) for r in range(world)], axis=1)
+        hs = [np.load(os.path.join(d, f"h{r}.npy")) for r in range(world)]
+    x = make_inputs(1, 16384, 512, torch.float32, seed=31, dist="c4", with_state=True)
+    args = [x[k] for k in ("u", "delta", "A", "Bm", "Cm", "Dv")]
+    o64, h64 = O.ss_fwd(*[np64(t) for t in args], np64(x["h_prev"]))
+    assert_fp32(out, o64, what="out")
+    for r in range(world):
+        assert_fp32(hs[r], h64, what=f"h_last on rank {r}")
