@@ -42,7 +42,8 @@ CONFIGS = {
                         "(SelectiveScanCuda, default V2 path)",
                B=4, L=2048, D=5120, dtype=torch.float16, mode="fwdbwd", dist="c3"),
     "c1": dict(workload="config 1: selective scan fwd+bwd fp32 B1 L1024 D256",
-               B=1, L=1024, D=256, dtype=torch.float32, mode="fwdbwd", dist="c1"),
+               B=1, L=1024, D=256, dtype=torch.float32, mode="fwdbwd", dist="c1",
+               metric="selective-scan fwd+bwd GB/s, B=1 L=1024 D=256 fp32"),
     "c2": dict(workload="config 2: Mamba-1.4B-like inference forward_with_state fp16",
                B=8, L=2048, D=4096, dtype=torch.float16, mode="fwd", dist="c2"),
     "c4": dict(workload="config 4: streaming scan fp32, 16 chunks of 65536 with h_prev/h_last "
@@ -277,7 +278,7 @@ def reference_arm(args, cfg):
                          "sample": desc},
         "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ----------------------------------------------------------------------------- GPU arms
@@ -467,7 +468,26 @@ def bench_stream(args, cfg, dev, world, rank, peaks):
                    "far above the 126 MB L2; no flush")
 
 
+_JSON_FD = None
+
+
+def emit(line):
+    """Write the one JSON result line to the process's original stdout."""
+    data = (json.dumps(line) + "\n").encode()
+    if _JSON_FD is None:
+        sys.stdout.write(data.decode())
+        sys.stdout.flush()
+    else:
+        os.write(_JSON_FD, data)
+
+
 def main():
+    global _JSON_FD
+    # Keep stdout for the JSON line alone: libraries that print banners to fd 1 (NCCL's
+    # version line, for one) are sent to stderr.
+    sys.stdout.flush()
+    _JSON_FD = os.dup(1)
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
@@ -518,7 +538,7 @@ def main():
         line["cpu_baseline"] = {"value": nbytes / secs / 1e9, "unit": "GB/s", "cores": threads,
                                 "kind": "port", "sample": desc}
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
