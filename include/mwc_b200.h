@@ -145,6 +145,26 @@ MWC_API int mwc_ss_fwd_noalloc(const void* u, const void* delta, const void* A, 
                                void* h_last, float* ckpt, float* decay,
                                int64_t B, int64_t L, int64_t D, int dtype, void* stream);
 
+/*
+ * mwc_check_last_launch -- waits for `stream` and reports whether the last persistent
+ * forward / backward kernel launched from this thread gave up on a bounded device wait
+ * (returns MWC_ERR_TIMEOUT, results of that call are invalid) or not (MWC_OK). The
+ * workspace passed to that call must still be allocated. Calls that ran the segmented
+ * kernels (which have no device waits) leave nothing to check: MWC_OK without touching
+ * the device. No counterpart in the reference (its kernels had no device-side waits).
+ */
+MWC_API int mwc_check_last_launch(void* stream);
+
+/*
+ * mwc_selftest_wait_timeout -- launches one CTA whose bounded mbarrier wait can never be
+ * satisfied (nothing arrives), with a short iteration limit, and reports what the host
+ * reads back: MWC_ERR_TIMEOUT is the expected outcome (the wait expired, the kernel
+ * recorded it in *dev_word and returned; the context stays usable), MWC_OK would mean the
+ * wait did not expire. `dev_word`: 4 bytes of device memory owned by the caller. For the
+ * failure-detection tests; no counterpart in the reference.
+ */
+MWC_API int mwc_selftest_wait_timeout(int* dev_word, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

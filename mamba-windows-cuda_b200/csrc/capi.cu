@@ -15,6 +15,7 @@
 #include "mwc_b200.h"
 #include "mwc_device.cuh"
 #include "mwc_internal.h"
+#include "mwc_tma.cuh"
 
 using namespace mwc;
 
@@ -24,6 +25,8 @@ using namespace mwc;
 namespace {
 
 thread_local char g_err[512] = "";
+// error word of the last persistent launch on this thread (nullptr: nothing to check)
+thread_local const int* g_last_err_word = nullptr;
 
 int fail(int code, const char* fmt, ...) {
     va_list ap;
@@ -132,6 +135,7 @@ int mwc_ss_fwd(const void* u, const void* delta, const void* A, const void* Bm, 
                const void* Dv, const void* h_prev, void* out, void* h_last, float* ckpt,
                float* decay, void* workspace, int64_t workspace_bytes, int64_t B, int64_t L,
                int64_t D, int dtype, void* stream) {
+    g_last_err_word = nullptr;
     int rc;
     if ((rc = check_dtype(dtype)) != MWC_OK) return rc;
     if ((rc = check_sizes(B, L, D)) != MWC_OK) return rc;
@@ -169,6 +173,7 @@ int mwc_ss_fwd(const void* u, const void* delta, const void* A, const void* Bm, 
             cudaError_t e = launch_fwd_persistent(pa, pp, dtype, workspace,
                                                   static_cast<cudaStream_t>(stream));
             if (e != cudaSuccess) return cuda_fail(e, "selective-scan persistent forward launch");
+            g_last_err_word = pa.err;
             return ok();
         }
     }
@@ -215,6 +220,7 @@ int mwc_ss_bwd(const void* u, const void* delta, const void* A, const void* Bm, 
                const float* ckpt, void* du, void* ddelta, void* dA, void* dB, void* dC, void* dD,
                void* dh_prev, void* workspace, int64_t workspace_bytes, int64_t B, int64_t L,
                int64_t D, int dtype, void* stream) {
+    g_last_err_word = nullptr;
     int rc;
     if ((rc = check_dtype(dtype)) != MWC_OK) return rc;
     if ((rc = check_sizes(B, L, D)) != MWC_OK) return rc;
@@ -257,6 +263,7 @@ int mwc_ss_bwd(const void* u, const void* delta, const void* A, const void* Bm, 
                 cudaError_t e = launch_bwd_persistent(pa, pb, dtype, workspace, dA, dB, dC, dD,
                                                       static_cast<cudaStream_t>(stream));
                 if (e != cudaSuccess) return cuda_fail(e, "selective-scan persistent backward launch");
+                g_last_err_word = pa.err;
                 return ok();
             }
         }
@@ -351,6 +358,35 @@ int mwc_lin_scan_bwd(const void* a, const void* h, const void* g, void* ga, void
     cudaError_t e = launch_lin_bwd(la, dtype, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "linear scan backward launch");
     return ok();
+}
+
+int mwc_check_last_launch(void* stream) {
+    const int* word = g_last_err_word;
+    if (word == nullptr) return ok();
+    cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "waiting for the stream");
+    int code = 0;
+    e = cudaMemcpy(&code, word, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(e, "reading the device error word");
+    if (code == 0) return ok();
+    return fail(MWC_ERR_TIMEOUT, "a bounded device wait of the last persistent kernel gave up "
+                "(code %d: %s); its results are invalid", code,
+                code == ERR_WAIT_TMA ? "pipeline barrier" :
+                code == ERR_WAIT_CHAIN ? "segment hand-off" :
+                code == ERR_SMEM_ALIGN ? "shared memory alignment" : "unknown");
+}
+
+int mwc_selftest_wait_timeout(int* dev_word, void* stream) {
+    if (dev_word == nullptr) return fail(MWC_ERR_INVALID, "dev_word is required");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemsetAsync(dev_word, 0, sizeof(int), s);
+    if (e == cudaSuccess) e = launch_wait_selftest(dev_word, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    int code = 0;
+    if (e == cudaSuccess) e = cudaMemcpy(&code, dev_word, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(e, "wait self-test");
+    if (code == ERR_WAIT_TMA) return fail(MWC_ERR_TIMEOUT, "self-test wait expired as intended");
+    return code == 0 ? ok() : fail(MWC_ERR_CUDA, "self-test recorded unexpected code %d", code);
 }
 
 }  // extern "C"

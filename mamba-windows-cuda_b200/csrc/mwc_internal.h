@@ -183,4 +183,8 @@ cudaError_t launch_bwd_final(const BwdFinalArgs& a, int dtype, cudaStream_t s);
 cudaError_t launch_lin_fwd(const LinArgs& a, int dtype, cudaStream_t s);
 cudaError_t launch_lin_bwd(const LinArgs& a, int dtype, cudaStream_t s);
 
+// One CTA waits on an mbarrier nothing arrives at, with a short bounded limit; records
+// ERR_WAIT_TMA in *err and returns (selftest.cu).
+cudaError_t launch_wait_selftest(int* err, cudaStream_t s);
+
 }  // namespace mwc

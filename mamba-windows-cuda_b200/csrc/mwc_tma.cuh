@@ -53,8 +53,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned phase) {
 }
 
 // Bounded wait for an mbarrier phase; records ERR_WAIT_TMA and returns false on expiry.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned phase, int* err) {
-    for (unsigned it = 0; it < WAIT_SPINS; ++it) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned phase, int* err,
+                                          unsigned limit = WAIT_SPINS) {
+    for (unsigned it = 0; it < limit; ++it) {
         if (mbar_try_wait(bar, phase)) return true;
         if (it > 64) __nanosleep(32);
         if ((it & (WAIT_POLL - 1)) == WAIT_POLL - 1 && wait_aborted(err)) return false;

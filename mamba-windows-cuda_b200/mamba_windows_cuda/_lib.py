@@ -36,6 +36,8 @@ SIGNATURES = {
     "mwc_lin_scan_fwd": (_int, [_vp] * 3 + [_i64] * 3 + [_int, _vp]),
     "mwc_lin_scan_bwd": (_int, [_vp] * 5 + [_i64] * 3 + [_int, _vp]),
     "mwc_ss_fwd_noalloc": (_int, [_vp] * 11 + [_i64] * 3 + [_int, _vp]),
+    "mwc_check_last_launch": (_int, [_vp]),
+    "mwc_selftest_wait_timeout": (_int, [_vp, _vp]),
 }
 
 _lock = threading.Lock()

@@ -10,6 +10,7 @@ and raises RuntimeError with the same messages.
 from __future__ import annotations
 
 import ctypes
+import os
 
 import torch
 
@@ -30,6 +31,16 @@ def dtype_code(t: torch.Tensor) -> int:
 
 def _p(t):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+# MWC_CHECK_WAITS=1: after every forward / backward call, wait for the stream and raise if a
+# bounded device wait of the persistent kernel gave up (costs a synchronisation per call).
+CHECK_WAITS = os.environ.get("MWC_CHECK_WAITS", "0") == "1"
+
+
+def _check_waits(lib, dev, what):
+    if CHECK_WAITS:
+        _lib.check(lib.mwc_check_last_launch(_stream(dev)), what)
 
 
 def _stream(device) -> ctypes.c_void_p:
@@ -122,6 +133,7 @@ def ss_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=None, *, want_out=True,
                             _p(h_prev), _p(out), _p(h_last), _p(ckpt), _p(decay), _p(ws),
                             ws_bytes, Bb, L, D, dt, _stream(dev))
     _lib.check(rc, "selective_scan forward")
+    _check_waits(lib, dev, "selective_scan forward")
     return out, h_last, ckpt, decay
 
 
@@ -158,6 +170,7 @@ def ss_backward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev, dout, dh_last, ckpt,
                             _p(dA), _p(dB), _p(dC), _p(dD), _p(dh_prev), _p(ws), ws_bytes,
                             Bb, L, D, dt, _stream(dev))
     _lib.check(rc, "selective_scan backward")
+    _check_waits(lib, dev, "selective_scan backward")
     return du, ddelta, dA, dB, dC, dD, dh_prev
 
 

@@ -89,6 +89,17 @@ def test_c_abi_rejects_bad_arguments_without_touching_the_gpu(lib):
     assert rc == 1
 
 
+def test_failure_entry_points_without_a_launch(lib):
+    # nothing launched on this thread (or the last call failed validation): nothing to
+    # check, and the device is not touched
+    fake = ctypes.c_void_p(16)
+    lib.mwc_ss_fwd(fake, fake, fake, fake, fake, fake, None, fake, None, None, None, None, 0,
+                   1, 16, 16, 7, None)
+    assert lib.mwc_check_last_launch(None) == 0
+    assert lib.mwc_selftest_wait_timeout(None, None) == 1
+    assert b"dev_word" in lib.mwc_last_error()
+
+
 def test_python_api_rejects_cpu_tensors_like_the_reference():
     import mamba_windows_cuda as m
     x = make_inputs(1, 8, 4)
