@@ -41,6 +41,10 @@ CONFIGS = {
     "c3": dict(workload="config 3: Mamba-2.8B-like training step, selective scan fwd+bwd "
                         "(SelectiveScanCuda, default V2 path)",
                B=4, L=2048, D=5120, dtype=torch.float16, mode="fwdbwd", dist="c3"),
+    "c3bf16": dict(workload="config 3 with bfloat16 I/O (an addition: the reference takes "
+                            "float32 / float16)",
+                   B=4, L=2048, D=5120, dtype=torch.bfloat16, mode="fwdbwd", dist="c3",
+                   metric="selective-scan fwd+bwd GB/s, B=4 L=2048 D=5120 bf16"),
     "c1": dict(workload="config 1: selective scan fwd+bwd fp32 B1 L1024 D256",
                B=1, L=1024, D=256, dtype=torch.float32, mode="fwdbwd", dist="c1",
                metric="selective-scan fwd+bwd GB/s, B=1 L=1024 D=256 fp32"),

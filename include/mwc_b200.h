@@ -16,8 +16,9 @@
  *   ckpt  : (B, nck, D, 16) float32, nck = mwc_ss_ckpt_count(L); ckpt[b, k] is the state
  *           after step min(16 (k + 1), L) - 1
  *   decay, h_in : (B, D, 16) float32
- * All floating tensors of one call share one dtype (MWC_F32 or MWC_F16) except the
- * float32 ckpt / decay / h_in buffers; arithmetic is float32 throughout.
+ * All floating tensors of one call share one dtype (MWC_F32, MWC_F16 or MWC_BF16) except
+ * the float32 ckpt / decay / h_in buffers; arithmetic is float32 throughout. (The
+ * reference takes float32 / float16; bfloat16 I/O is an addition of this library.)
  *
  * Return value: MWC_OK (0) or an MWC_ERR_* code; mwc_last_error() then gives the message
  * (same wording as the reference's TORCH_CHECKs where one exists).
@@ -39,7 +40,7 @@ extern "C" {
 #define MWC_API
 #endif
 
-enum mwc_dtype { MWC_F32 = 0, MWC_F16 = 1 };
+enum mwc_dtype { MWC_F32 = 0, MWC_F16 = 1, MWC_BF16 = 2 };
 
 enum mwc_status {
     MWC_OK = 0,

@@ -57,7 +57,7 @@ int device_sms() {
     return n;
 }
 
-size_t elem_size(int dtype) { return dtype == MWC_F16 ? 2 : 4; }
+size_t elem_size(int dtype) { return dtype == MWC_F32 ? 4 : 2; }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -81,8 +81,8 @@ BwdWs bwd_ws(int64_t B, int64_t L, int64_t D, int dtype) {
 }
 
 int check_dtype(int dtype) {
-    if (dtype != MWC_F32 && dtype != MWC_F16)
-        return fail(MWC_ERR_INVALID, "u must be float32/float16 (dtype code %d)", dtype);
+    if (dtype != MWC_F32 && dtype != MWC_F16 && dtype != MWC_BF16)
+        return fail(MWC_ERR_INVALID, "u must be float32/float16/bfloat16 (dtype code %d)", dtype);
     return MWC_OK;
 }
 

@@ -71,8 +71,8 @@ extern "C" MWC_API int mwc_ss_fwd_noalloc(const void* u, const void* delta, cons
                                           const void* h_prev, void* out, void* h_last,
                                           float* ckpt, float* decay, int64_t B, int64_t L,
                                           int64_t D, int dtype, void* stream) {
-    if (dtype != MWC_F32 && dtype != MWC_F16)
-        return report_error(MWC_ERR_INVALID, "u must be float32/float16");
+    if (dtype != MWC_F32 && dtype != MWC_F16 && dtype != MWC_BF16)
+        return report_error(MWC_ERR_INVALID, "u must be float32/float16/bfloat16");
     if (B < 0 || L < 0 || D < 0) return report_error(MWC_ERR_INVALID, "negative size");
     if (L == 0) return report_error(MWC_ERR_INVALID, "empty sequence (L=0)");
     if (B > 65535) return report_error(MWC_ERR_UNSUPPORTED, "batch exceeds 65535");
@@ -96,7 +96,7 @@ extern "C" MWC_API int mwc_ss_fwd_noalloc(const void* u, const void* delta, cons
         if (rc != MWC_OK) return rc;
     }
 
-    const size_t es = dtype == MWC_F16 ? 2 : 4;
+    const size_t es = dtype == MWC_F32 ? 4 : 2;
     FwdArgs a{};
     a.u = u; a.delta = delta; a.A = A; a.Bm = Bm; a.Cm = Cm; a.Dv = Dv;
     a.h_prev = h_prev; a.out = out; a.h_last = h_last; a.ckpt = ckpt; a.decay = decay;

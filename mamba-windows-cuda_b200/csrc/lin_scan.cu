@@ -209,10 +209,12 @@ static cudaError_t launch_lin_t(const LinArgs& a, bool fwd, cudaStream_t s) {
 }
 
 cudaError_t launch_lin_fwd(const LinArgs& a, int dtype, cudaStream_t s) {
+    if (dtype == 2) return launch_lin_t<__nv_bfloat16>(a, true, s);
     return dtype == 1 ? launch_lin_t<__half>(a, true, s) : launch_lin_t<float>(a, true, s);
 }
 
 cudaError_t launch_lin_bwd(const LinArgs& a, int dtype, cudaStream_t s) {
+    if (dtype == 2) return launch_lin_t<__nv_bfloat16>(a, false, s);
     return dtype == 1 ? launch_lin_t<__half>(a, false, s) : launch_lin_t<float>(a, false, s);
 }
 

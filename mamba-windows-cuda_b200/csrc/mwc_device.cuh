@@ -1,6 +1,7 @@
 // Device-side helpers shared by the selective-scan and linear-scan kernels (sm_100a).
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
 
@@ -25,14 +26,17 @@ __device__ __forceinline__ float ex2(float x) {
 
 __device__ __forceinline__ float to_f(float x) { return x; }
 __device__ __forceinline__ float to_f(__half x) { return __half2float(x); }
+__device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
 
 template <typename T> __device__ __forceinline__ T from_f(float x);
 template <> __device__ __forceinline__ float from_f<float>(float x) { return x; }
 template <> __device__ __forceinline__ __half from_f<__half>(float x) { return __float2half_rn(x); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
 
 template <typename T> __device__ __forceinline__ T zero_v();
 template <> __device__ __forceinline__ float zero_v<float>() { return 0.f; }
 template <> __device__ __forceinline__ __half zero_v<__half>() { return __float2half_rn(0.f); }
+template <> __device__ __forceinline__ __nv_bfloat16 zero_v<__nv_bfloat16>() { return __float2bfloat16_rn(0.f); }
 
 // Copy a ROWS x COLS tile of a row-major matrix (row stride ld elements) into shared
 // memory, zero-filling rows >= nrows and columns >= ncols. When `vec` holds (uniform per

@@ -255,7 +255,8 @@ int bwd_channels_per_block(int dtype) {
 cudaError_t launch_bwd(const BwdArgs& a, int dtype, cudaStream_t s) {
     constexpr int CPB = BWD_NW * (32 / (NSTATE / BWD_S));
     dim3 grid((unsigned)((a.D + CPB - 1) / CPB), (unsigned)a.B, 1);
-    if (dtype == 1) ss_bwd_kernel<__half, BWD_S, BWD_NW><<<grid, BWD_NW * 32, 0, s>>>(a);
+    if (dtype == 2) ss_bwd_kernel<__nv_bfloat16, BWD_S, BWD_NW><<<grid, BWD_NW * 32, 0, s>>>(a);
+    else if (dtype == 1) ss_bwd_kernel<__half, BWD_S, BWD_NW><<<grid, BWD_NW * 32, 0, s>>>(a);
     else ss_bwd_kernel<float, BWD_S, BWD_NW><<<grid, BWD_NW * 32, 0, s>>>(a);
     return cudaGetLastError();
 }
@@ -266,7 +267,8 @@ cudaError_t launch_bwd_final(const BwdFinalArgs& a, int dtype, cudaStream_t s) {
     int64_t blocks = (total + threads - 1) / threads;
     if (blocks > 148 * 8) blocks = 148 * 8;
     if (blocks < 1) blocks = 1;
-    if (dtype == 1) ss_bwd_final_kernel<__half><<<(unsigned)blocks, threads, 0, s>>>(a);
+    if (dtype == 2) ss_bwd_final_kernel<__nv_bfloat16><<<(unsigned)blocks, threads, 0, s>>>(a);
+    else if (dtype == 1) ss_bwd_final_kernel<__half><<<(unsigned)blocks, threads, 0, s>>>(a);
     else ss_bwd_final_kernel<float><<<(unsigned)blocks, threads, 0, s>>>(a);
     return cudaGetLastError();
 }

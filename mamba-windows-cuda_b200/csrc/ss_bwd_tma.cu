@@ -103,6 +103,12 @@ __device__ __forceinline__ void load2<__half>(float (&v)[2], const __half* p) {
     v[0] = a.x; v[1] = a.y;
 }
 
+template <>
+__device__ __forceinline__ void load2<__nv_bfloat16>(float (&v)[2], const __nv_bfloat16* p) {
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+    v[0] = a.x; v[1] = a.y;
+}
+
 template <typename T>
 __device__ __forceinline__ void load4(float (&v)[4], const T* p);
 template <>
@@ -118,6 +124,14 @@ __device__ __forceinline__ void load4<__half>(float (&v)[4], const __half* p) {
     v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
 }
 
+template <>
+__device__ __forceinline__ void load4<__nv_bfloat16>(float (&v)[4], const __nv_bfloat16* p) {
+    const uint2 raw = *reinterpret_cast<const uint2*>(p);
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+    v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+}
+
 template <typename T>
 __device__ __forceinline__ void store2(T* p, float a, float b);
 template <>
@@ -127,6 +141,11 @@ __device__ __forceinline__ void store2<float>(float* p, float a, float b) {
 template <>
 __device__ __forceinline__ void store2<__half>(__half* p, float a, float b) {
     *reinterpret_cast<__half2*>(p) = __floats2half2_rn(a, b);
+}
+
+template <>
+__device__ __forceinline__ void store2<__nv_bfloat16>(__nv_bfloat16* p, float a, float b) {
+    *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(a, b);
 }
 
 template <typename T>
@@ -139,6 +158,15 @@ template <>
 __device__ __forceinline__ void store4<__half>(__half* p, const float (&v)[4]) {
     __half2 a = __floats2half2_rn(v[0], v[1]);
     __half2 b = __floats2half2_rn(v[2], v[3]);
+    uint2 raw;
+    raw.x = *reinterpret_cast<uint32_t*>(&a);
+    raw.y = *reinterpret_cast<uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(p) = raw;
+}
+template <>
+__device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16* p, const float (&v)[4]) {
+    __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]);
+    __nv_bfloat162 b = __floats2bfloat162_rn(v[2], v[3]);
     uint2 raw;
     raw.x = *reinterpret_cast<uint32_t*>(&a);
     raw.y = *reinterpret_cast<uint32_t*>(&b);
@@ -768,7 +796,8 @@ BwdPersistWs bwd_persistent_ws(const PersistPlan& pl, int64_t B, int64_t L) {
     return w;
 }
 
-static_assert(sizeof(PBwdSmem<float>) <= 227 * 1024 && sizeof(PBwdSmem<__half>) <= 227 * 1024,
+static_assert(sizeof(PBwdSmem<float>) <= 227 * 1024 && sizeof(PBwdSmem<__half>) <= 227 * 1024 &&
+                  sizeof(PBwdSmem<__nv_bfloat16>) <= 227 * 1024,
               "backward shared memory exceeds the 227 KB a CTA may use");
 
 template <typename T>
@@ -807,6 +836,7 @@ cudaError_t launch_bwd_persistent(PBwdArgs& a, const PersistPlan& pl, int dtype,
     a.ntiles = pl.ntiles;
     cudaError_t e = cudaMemsetAsync(ws, 0, (size_t)w.off_hand, s);
     if (e != cudaSuccess) return e;
+    if (dtype == 2) return launch_pb<__nv_bfloat16>(a, pl.grid, dA, dB, dC, dD, s);
     return dtype == 1 ? launch_pb<__half>(a, pl.grid, dA, dB, dC, dD, s)
                       : launch_pb<float>(a, pl.grid, dA, dB, dC, dD, s);
 }

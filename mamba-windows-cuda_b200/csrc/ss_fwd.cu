@@ -345,10 +345,12 @@ static cudaError_t launch_fixup_s(const FixupArgs& a, const FwdPlan& plan, cudaS
 }
 
 cudaError_t launch_fwd(const FwdArgs& a, const FwdPlan& plan, int dtype, cudaStream_t s) {
+    if (dtype == 2) return launch_fwd_s<__nv_bfloat16>(a, plan, s);
     return dtype == 1 ? launch_fwd_s<__half>(a, plan, s) : launch_fwd_s<float>(a, plan, s);
 }
 
 cudaError_t launch_fixup(const FixupArgs& a, const FwdPlan& plan, int dtype, cudaStream_t s) {
+    if (dtype == 2) return launch_fixup_s<__nv_bfloat16>(a, plan, s);
     return dtype == 1 ? launch_fixup_s<__half>(a, plan, s) : launch_fixup_s<float>(a, plan, s);
 }
 

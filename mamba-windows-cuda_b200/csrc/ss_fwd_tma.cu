@@ -399,12 +399,13 @@ bool make_tmap_3d(CUtensorMap* map, const void* base, int dtype, int64_t W, int6
                   int64_t B, int bw, int bl) {
     auto fn = encode_fn();
     if (fn == nullptr) return false;
-    const size_t es = dtype == 1 ? 2 : 4;
+    const size_t es = dtype == 0 ? 4 : 2;
     cuuint64_t dims[3] = {(cuuint64_t)W, (cuuint64_t)L, (cuuint64_t)B};
     cuuint64_t strides[2] = {(cuuint64_t)(W * es), (cuuint64_t)(W * L * es)};
     cuuint32_t box[3] = {(cuuint32_t)bw, (cuuint32_t)bl, 1};
     cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = fn(map, dtype == 1 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+    CUresult r = fn(map, dtype == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                         : dtype == 1 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
                     3, const_cast<void*>(base), dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -474,6 +475,7 @@ cudaError_t launch_fwd_persistent(PFwdArgs& a, const PersistPlan& pl, int dtype,
     a.ntiles = pl.ntiles;
     cudaError_t e = cudaMemsetAsync(ws, 0, (size_t)persistent_ws_header(pl), s);
     if (e != cudaSuccess) return e;
+    if (dtype == 2) return launch_pf<__nv_bfloat16>(a, pl.grid, s);
     return dtype == 1 ? launch_pf<__half>(a, pl.grid, s) : launch_pf<float>(a, pl.grid, s);
 }
 

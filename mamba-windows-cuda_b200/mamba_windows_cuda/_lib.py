@@ -14,6 +14,7 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", LIB_
 
 MWC_F32 = 0
 MWC_F16 = 1
+MWC_BF16 = 2
 MWC_OK = 0
 STATUS_NAMES = {1: "invalid argument", 2: "unsupported", 3: "workspace", 4: "CUDA error",
                 5: "device wait timed out"}

@@ -19,14 +19,15 @@ from . import _lib
 NSTATE = 16
 CK = 16
 
-_DTYPES = {torch.float32: _lib.MWC_F32, torch.float16: _lib.MWC_F16}
+_DTYPES = {torch.float32: _lib.MWC_F32, torch.float16: _lib.MWC_F16,
+           torch.bfloat16: _lib.MWC_BF16}
 
 
 def dtype_code(t: torch.Tensor) -> int:
     try:
         return _DTYPES[t.dtype]
     except KeyError:
-        raise RuntimeError("u must be float32/float16") from None
+        raise RuntimeError("u must be float32/float16/bfloat16") from None
 
 
 def _p(t):
@@ -55,7 +56,7 @@ def check_ss_inputs(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=None):
         if not isinstance(t, torch.Tensor) or not t.is_cuda:
             raise RuntimeError(f"{name} must be a CUDA tensor")
     if u.dtype not in _DTYPES:
-        raise RuntimeError("u must be float32/float16")
+        raise RuntimeError("u must be float32/float16/bfloat16")
     for name, t in named[1:]:
         if t.dtype != u.dtype:
             raise RuntimeError(f"{name} dtype must match u dtype")

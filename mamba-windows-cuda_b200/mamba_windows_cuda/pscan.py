@@ -19,8 +19,8 @@ def _check(A, X):
     for name, t in (("A", A), ("X", X)):
         if not isinstance(t, torch.Tensor) or not t.is_cuda:
             raise RuntimeError(f"{name} must be a CUDA tensor")
-    if X.dtype not in (torch.float32, torch.float16):
-        raise RuntimeError("X must be float32/float16")
+    if X.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+        raise RuntimeError("X must be float32/float16/bfloat16")
     if A.dtype != X.dtype:
         raise RuntimeError("A dtype must match X dtype")
     if X.dim() != 4 or A.shape != X.shape:
