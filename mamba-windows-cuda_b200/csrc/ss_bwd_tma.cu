@@ -30,6 +30,7 @@
 #include "mwc_tma.cuh"
 
 #include <algorithm>
+#include <type_traits>
 
 namespace mwc {
 
@@ -75,6 +76,7 @@ struct __align__(128) PBwdSmem {
     uint64_t redfull[C::RB], redempty[C::RB], ofull[2], oempty[2];
     int unit[PB_ST];
     int tile[PB_ST];
+    int dpos[PB_ST];   // helper: 1 when no delta of the stage's tile has its sign bit set
     uint32_t tmem_base;
 };
 
@@ -306,6 +308,21 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                         (&s.Cf[HALF ? st : 0][0][0])[idx] = to_f((&s.Ct[st][0][0])[idx]);
                     }
                 }
+                // safe_exp's clamp is the identity for the whole tile when no delta is
+                // negative (given A <= 0): OR of the raw sign bits of the delta tile
+                const uint4* dw = reinterpret_cast<const uint4*>(&s.d[st][0][0]);
+                constexpr int NW4 = PB_LT * PB_CPB * (int)sizeof(T) / 16;
+                constexpr uint32_t SIGN = sizeof(T) == 2 ? 0x80008000u : 0x80000000u;
+                uint32_t neg = 0;
+#pragma unroll 4
+                for (int idx = lane; idx < NW4; idx += 32) {
+                    const uint4 v = dw[idx];
+                    neg |= (v.x | v.y | v.z | v.w) & SIGN;
+                }
+                const bool any_neg = __any_sync(FULL, neg != 0);
+                if (lane == 0) s.dpos[st] = any_neg ? 0 : 1;
+            } else if (lane == 0) {
+                s.dpos[st] = 0;
             }
             __syncwarp();
             if (lane == 0) mbar_arrive_b(&s.conv[st]);
@@ -431,6 +448,11 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
         //      h ends as the state after the last step (blocks of 4 steps: loads, then the
         //      serial updates) ----
         __syncwarp();   // the chunk-start loads above depend on the channel's lane
+        // safe_exp's clamp is the identity when every exponent is <= 0: A <= 0 for the unit
+        // and no negative delta in the tile (uniform per tile)
+        // (each copy of the recompute loop below is branch-free)
+        auto recompute = [&](auto clamp_tag) {
+            constexpr bool CLAMP = decltype(clamp_tag)::value;
 #pragma unroll 1
         for (int i0 = 0; i0 < PB_LT; i0 += 4) {
             float dt[4][2], uu[4][2];
@@ -441,11 +463,6 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                 load2<T>(uu[r], &s.u[st][i0 + r][c2]);
                 B4[r] = *reinterpret_cast<const float4*>(Bf + (i0 + r) * NSTATE + 4 * sg);
             }
-            float dmin = INFINITY;
-#pragma unroll
-            for (int r = 0; r < 4; ++r) dmin = fminf(dmin, fminf(dt[r][0], dt[r][1]));
-            // safe_exp's clamp is the identity when every exponent is <= 0
-            const bool fast = a_nonpos && __all_sync(FULL, dmin >= 0.f);
             float2 x[4][2][2];
 #pragma unroll
             for (int r = 0; r < 4; ++r)
@@ -454,7 +471,7 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                     x[r][cc][0] = __fmul2_rn(f2(dt[r][cc]), A2[cc][0]);
                     x[r][cc][1] = __fmul2_rn(f2(dt[r][cc]), A2[cc][1]);
                 }
-            if (!fast) {
+            if constexpr (CLAMP) {
 #pragma unroll
                 for (int r = 0; r < 4; ++r)
 #pragma unroll
@@ -487,6 +504,11 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                 tmem_st16(tcache + (uint32_t)(i0 + r) * 16u, tv);
             }
         }
+        };
+        if (a_nonpos && s.dpos[st] != 0)
+            recompute(std::false_type{});
+        else
+            recompute(std::true_type{});
         tmem_wait_st();   // the adjoint pass reads these columns back
 
         if (pc == 0 && kp > 0) {

@@ -26,6 +26,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <type_traits>
 
 namespace mwc {
 
@@ -60,6 +61,7 @@ struct __align__(128) PFwdSmem {
     uint64_t full[ST], conv[ST], empty[ST], yfull[2], yempty[2];
     int unit[ST];
     int tile[ST];
+    int dpos[ST];   // helper: 1 when no delta of the stage's tile has its sign bit set
 };
 
 // One block of 8 steps for the lane's 8 states (4 float2 pairs). CLAMP applies the
@@ -113,7 +115,9 @@ __device__ __forceinline__ void bulk_load_1d(void* dst, const void* src, unsigne
         : "memory");
 }
 
-template <typename T>
+// DECAY: the launch asks for the segment decay, so each lane also sums its channel's delta
+// (and passes the sum between segments); without it that work is compiled out.
+template <typename T, bool DECAY>
 __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __grid_constant__ PFwdArgs p) {
     // Direct cast (no integer round trip): accesses stay in the shared address space.
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -223,6 +227,21 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
                         if (p.has_out) (&s.Cf[st][0][0])[idx] = to_f((&s.Ct[st][0][0])[idx]);
                     }
                 }
+                // safe_exp's clamp is the identity for the whole tile when no delta is
+                // negative (given A <= 0): OR of the raw sign bits of the delta tile
+                const uint4* dw = reinterpret_cast<const uint4*>(&s.d[st][0][0]);
+                constexpr int NW4 = PF_LT * PF_CPB * (int)sizeof(T) / 16;
+                constexpr uint32_t SIGN = sizeof(T) == 2 ? 0x80008000u : 0x80000000u;
+                uint32_t neg = 0;
+#pragma unroll 4
+                for (int idx = lane; idx < NW4; idx += 32) {
+                    const uint4 v = dw[idx];
+                    neg |= (v.x | v.y | v.z | v.w) & SIGN;
+                }
+                const bool any_neg = __any_sync(FULL, neg != 0);
+                if (lane == 0) s.dpos[st] = any_neg ? 0 : 1;
+            } else if (lane == 0) {
+                s.dpos[st] = 0;
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&s.conv[st]);
@@ -304,21 +323,21 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
         const int yb = it & 1;
         if (p.has_out) mbar_wait(&s.yempty[yb], ((unsigned)(it / 2) & 1u) ^ 1u, p.err);
 
+        // The tile's steps; CLAMP is uniform per tile (A <= 0 for the unit and no negative
+        // delta in the tile make the clamp the identity), so each copy of the loop is
+        // branch-free.
+        auto run_tile = [&](auto clamp_tag) {
+            constexpr bool CLAMP = decltype(clamp_tag)::value;
 #pragma unroll 1
         for (int i0 = 0; i0 < PF_LT; i0 += 8) {
             float dtv[8], uv[8], yv[8];
-            float dmin = INFINITY;
 #pragma unroll
             for (int r = 0; r < 8; ++r) {
                 dtv[r] = to_f(s.d[st][i0 + r][ch]);
                 uv[r] = to_f(s.u[st][i0 + r][ch]);
-                dmin = fminf(dmin, dtv[r]);
-                sumd += dtv[r];
+                if constexpr (DECAY) sumd += dtv[r];
             }
-            if (a_nonpos && __all_sync(FULL, dmin >= 0.f))
-                fwd_block8<false>(h2, A2v, dtv, uv, Bf + i0 * NSTATE, Cf + i0 * NSTATE, n0, yv);
-            else
-                fwd_block8<true>(h2, A2v, dtv, uv, Bf + i0 * NSTATE, Cf + i0 * NSTATE, n0, yv);
+            fwd_block8<CLAMP>(h2, A2v, dtv, uv, Bf + i0 * NSTATE, Cf + i0 * NSTATE, n0, yv);
             if (p.has_out) {
 #pragma unroll
                 for (int r = 0; r < 8; ++r) {
@@ -336,6 +355,11 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
                 }
             }
         }
+        };
+        if (a_nonpos && s.dpos[st] != 0)
+            run_tile(std::false_type{});
+        else
+            run_tile(std::true_type{});
         // this warp is done with the stage's inputs and with its rows of the y tile
         __syncwarp();
         if (lane == 0) mbar_arrive(&s.empty[st]);
@@ -451,14 +475,19 @@ int64_t persistent_ws_header(const PersistPlan& pl) {
     return ((16 + units * 4) + 255) / 256 * 256;
 }
 
-template <typename T>
-static cudaError_t launch_pf(const PFwdArgs& a, int grid, cudaStream_t s) {
+template <typename T, bool DECAY>
+static cudaError_t launch_pf_t(const PFwdArgs& a, int grid, cudaStream_t s) {
     const size_t smem = sizeof(PFwdSmem<T>);
-    cudaError_t e = cudaFuncSetAttribute(ss_fwd_persistent_kernel<T>,
+    cudaError_t e = cudaFuncSetAttribute(ss_fwd_persistent_kernel<T, DECAY>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    ss_fwd_persistent_kernel<T><<<grid, PF_NT, smem, s>>>(a);
+    ss_fwd_persistent_kernel<T, DECAY><<<grid, PF_NT, smem, s>>>(a);
     return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t launch_pf(const PFwdArgs& a, int grid, cudaStream_t s) {
+    return a.decay != nullptr ? launch_pf_t<T, true>(a, grid, s) : launch_pf_t<T, false>(a, grid, s);
 }
 
 cudaError_t launch_fwd_persistent(PFwdArgs& a, const PersistPlan& pl, int dtype, void* ws,
