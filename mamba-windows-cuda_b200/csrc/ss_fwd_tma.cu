@@ -35,6 +35,7 @@ constexpr int PF_CPB = 128;
 constexpr int PF_NCW = 8;                    // compute warps
 constexpr int PF_NT = (PF_NCW + 2) * 32;     // + producer warp + helper warp
 constexpr int PF_HAND = PF_CPB * (NSTATE + 1);  // floats of one segment hand-off record
+static_assert(PF_LT % CK == 0, "a forward tile holds whole checkpoint chunks");
 #ifndef MWC_FWD_MIN_SEG_TILES
 #define MWC_FWD_MIN_SEG_TILES 2   // shortest segment (in 32-step tiles) the planner may pick
 #endif
@@ -326,40 +327,51 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
         // The tile's steps; CLAMP is uniform per tile (A <= 0 for the unit and no negative
         // delta in the tile make the clamp the identity), so each copy of the loop is
         // branch-free.
-        auto run_tile = [&](auto clamp_tag) {
+        // The tile's steps as 16-step chunks of two 8-step blocks (a checkpoint after each
+        // chunk). CLAMP and HAS_OUT are uniform (CLAMP per tile: A <= 0 for the unit and no
+        // negative delta in the tile make the clamp the identity), so each copy of the loop
+        // is branch-free.
+        const bool want_ck = p.ckpt != nullptr;
+        auto run_tile = [&](auto clamp_tag, auto out_tag) {
             constexpr bool CLAMP = decltype(clamp_tag)::value;
+            constexpr bool HAS_OUT = decltype(out_tag)::value;
 #pragma unroll 1
-        for (int i0 = 0; i0 < PF_LT; i0 += 8) {
-            float dtv[8], uv[8], yv[8];
+            for (int c0 = 0; c0 < PF_LT; c0 += CK) {
 #pragma unroll
-            for (int r = 0; r < 8; ++r) {
-                dtv[r] = to_f(s.d[st][i0 + r][ch]);
-                uv[r] = to_f(s.u[st][i0 + r][ch]);
-                if constexpr (DECAY) sumd += dtv[r];
-            }
-            fwd_block8<CLAMP>(h2, A2v, dtv, uv, Bf + i0 * NSTATE, Cf + i0 * NSTATE, n0, yv);
-            if (p.has_out) {
+                for (int i0 = c0; i0 < c0 + CK; i0 += 8) {
+                    float dtv[8], uv[8], yv[8];
 #pragma unroll
-                for (int r = 0; r < 8; ++r) {
-                    const float y = yv[r] + __shfl_xor_sync(FULL, yv[r], 1);
-                    if (half == 0) s.y[yb][i0 + r][ch] = from_f<T>(fmaf(Dd, uv[r], y));
+                    for (int r = 0; r < 8; ++r) {
+                        dtv[r] = to_f(s.d[st][i0 + r][ch]);
+                        uv[r] = to_f(s.u[st][i0 + r][ch]);
+                        if constexpr (DECAY) sumd += dtv[r];
+                    }
+                    fwd_block8<CLAMP>(h2, A2v, dtv, uv, Bf + i0 * NSTATE, Cf + i0 * NSTATE, n0, yv);
+                    if constexpr (HAS_OUT) {
+#pragma unroll
+                        for (int r = 0; r < 8; ++r) {
+                            const float y = yv[r] + __shfl_xor_sync(FULL, yv[r], 1);
+                            if (half == 0) s.y[yb][i0 + r][ch] = from_f<T>(fmaf(Dd, uv[r], y));
+                        }
+                    }
                 }
-            }
-            if ((i0 + 8) % CK == 0 && p.ckpt != nullptr) {
-                const int64_t kk = (int64_t)(t0 + i0 + 8) / CK - 1;
-                if (kk < p.nck && dv) {
+                const int64_t kk = (int64_t)(t0 + c0) / CK;
+                if (want_ck && kk < p.nck && dv) {
                     float4* cp = reinterpret_cast<float4*>(
                         p.ckpt + (((int64_t)b * p.nck + kk) * p.D + d) * NSTATE + n0);
                     cp[0] = make_float4(h2[0].x, h2[0].y, h2[1].x, h2[1].y);
                     cp[1] = make_float4(h2[2].x, h2[2].y, h2[3].x, h2[3].y);
                 }
             }
-        }
         };
-        if (a_nonpos && s.dpos[st] != 0)
-            run_tile(std::false_type{});
-        else
-            run_tile(std::true_type{});
+        const bool clamp = !(a_nonpos && s.dpos[st] != 0);
+        if (p.has_out) {
+            if (clamp) run_tile(std::true_type{}, std::true_type{});
+            else run_tile(std::false_type{}, std::true_type{});
+        } else {
+            if (clamp) run_tile(std::true_type{}, std::false_type{});
+            else run_tile(std::false_type{}, std::false_type{});
+        }
         // this warp is done with the stage's inputs and with its rows of the y tile
         __syncwarp();
         if (lane == 0) mbar_arrive(&s.empty[st]);
