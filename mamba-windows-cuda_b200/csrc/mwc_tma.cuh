@@ -156,6 +156,23 @@ __device__ __forceinline__ void tmem_wait_ld(uint32_t (&v)[16]) {
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;"); }
 
+// One wait for four outstanding x16 loads (all 64 registers pass through it).
+__device__ __forceinline__ void tmem_wait_ld4(uint32_t (&v)[4][16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(v[0][0]), "+r"(v[0][1]), "+r"(v[0][2]), "+r"(v[0][3]), "+r"(v[0][4]), "+r"(v[0][5]),
+                   "+r"(v[0][6]), "+r"(v[0][7]), "+r"(v[0][8]), "+r"(v[0][9]), "+r"(v[0][10]), "+r"(v[0][11]),
+                   "+r"(v[0][12]), "+r"(v[0][13]), "+r"(v[0][14]), "+r"(v[0][15]),
+                   "+r"(v[1][0]), "+r"(v[1][1]), "+r"(v[1][2]), "+r"(v[1][3]), "+r"(v[1][4]), "+r"(v[1][5]),
+                   "+r"(v[1][6]), "+r"(v[1][7]), "+r"(v[1][8]), "+r"(v[1][9]), "+r"(v[1][10]), "+r"(v[1][11]),
+                   "+r"(v[1][12]), "+r"(v[1][13]), "+r"(v[1][14]), "+r"(v[1][15]),
+                   "+r"(v[2][0]), "+r"(v[2][1]), "+r"(v[2][2]), "+r"(v[2][3]), "+r"(v[2][4]), "+r"(v[2][5]),
+                   "+r"(v[2][6]), "+r"(v[2][7]), "+r"(v[2][8]), "+r"(v[2][9]), "+r"(v[2][10]), "+r"(v[2][11]),
+                   "+r"(v[2][12]), "+r"(v[2][13]), "+r"(v[2][14]), "+r"(v[2][15]),
+                   "+r"(v[3][0]), "+r"(v[3][1]), "+r"(v[3][2]), "+r"(v[3][3]), "+r"(v[3][4]), "+r"(v[3][5]),
+                   "+r"(v[3][6]), "+r"(v[3][7]), "+r"(v[3][8]), "+r"(v[3][9]), "+r"(v[3][10]), "+r"(v[3][11]),
+                   "+r"(v[3][12]), "+r"(v[3][13]), "+r"(v[3][14]), "+r"(v[3][15]));
+}
+
 // Thread i of the warp writes / reads 16 consecutive 32-bit columns of lane (taddr lane + i).
 // These touch tensor memory and registers only: no "memory" clobber, so shared / global
 // loads may be scheduled across them. Their order among themselves is that of the volatile

@@ -548,11 +548,11 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                 load2<T>(gy[r], &s.g[st][i0 + r][c2]);
             }
             uint32_t tv[4][16];   // per step: state before the step, then its decay factors
-            __syncwarp();         // the output stores of the previous block may diverge
+            // only the float32 path's direct output stores diverge inside this loop
+            if constexpr (!Cfg::STAGE_OUT) __syncwarp();
 #pragma unroll
             for (int r = 0; r < 4; ++r) tmem_ld16(tcache + (uint32_t)(i0 + r) * 16u, tv[r]);
-#pragma unroll
-            for (int r = 0; r < 4; ++r) tmem_wait_ld(tv[r]);
+            tmem_wait_ld4(tv);
             float vv[4][8];   // per step: dB partial (states 4sg..4sg+3), then dC partial
             float sv[4][4];   // per step: S1 (channels c2, c2+1), then S2
 #pragma unroll
