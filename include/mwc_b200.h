@@ -147,6 +147,34 @@ MWC_API int mwc_ss_fwd_noalloc(const void* u, const void* delta, const void* A, 
                                int64_t B, int64_t L, int64_t D, int dtype, void* stream);
 
 /*
+ * Extended scan with the input / output transforms of Mamba's block (not in the reference,
+ * which takes delta and returns y as they are; the official Mamba scan has these arguments):
+ *   delta_eff = softplus(delta + delta_bias)   if delta_softplus, else delta + delta_bias
+ *               (delta_bias: (D), NULL = 0; softplus(x) = log(1 + e^x), x for x > 20)
+ *   out       = the selective scan of (u, delta_eff, A, Bm, Cm, Dv, h_prev)   (ungated y)
+ *   out_z     = out * silu(z) = out * z / (1 + e^-z)          when z (B, L, D) is given
+ * The backward takes dout with respect to out_z when z is given (else to out), the ungated
+ * `out` of the forward (required with z) and returns dz and ddelta_bias (D) (both may be
+ * NULL when not wanted). Layouts, dtypes and the other arguments as mwc_ss_fwd / _bwd;
+ * ckpt is the forward's checkpoint buffer. Workspaces: the _workspace_bytes queries.
+ */
+MWC_API int64_t mwc_ss_fwd_ex_workspace_bytes(int64_t B, int64_t L, int64_t D, int dtype);
+MWC_API int mwc_ss_fwd_ex(const void* u, const void* delta, const void* A, const void* Bm,
+                          const void* Cm, const void* Dv, const void* z, const void* delta_bias,
+                          int delta_softplus, const void* h_prev, void* out, void* out_z,
+                          void* h_last, float* ckpt, void* workspace, int64_t workspace_bytes,
+                          int64_t B, int64_t L, int64_t D, int dtype, void* stream);
+MWC_API int64_t mwc_ss_bwd_ex_workspace_bytes(int64_t B, int64_t L, int64_t D, int dtype);
+MWC_API int mwc_ss_bwd_ex(const void* u, const void* delta, const void* A, const void* Bm,
+                          const void* Cm, const void* Dv, const void* z, const void* delta_bias,
+                          int delta_softplus, const void* h_prev, const void* out,
+                          const void* dout, const void* dh_last, const float* ckpt, void* du,
+                          void* ddelta, void* dA, void* dB, void* dC, void* dD,
+                          void* ddelta_bias, void* dz, void* dh_prev, void* workspace,
+                          int64_t workspace_bytes, int64_t B, int64_t L, int64_t D, int dtype,
+                          void* stream);
+
+/*
  * mwc_check_last_launch -- waits for `stream` and reports whether the last persistent
  * forward / backward kernel launched from this thread gave up on a bounded device wait
  * (returns MWC_ERR_TIMEOUT, results of that call are invalid) or not (MWC_OK). The

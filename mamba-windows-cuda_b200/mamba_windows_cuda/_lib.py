@@ -37,6 +37,10 @@ SIGNATURES = {
     "mwc_lin_scan_fwd": (_int, [_vp] * 3 + [_i64] * 3 + [_int, _vp]),
     "mwc_lin_scan_bwd": (_int, [_vp] * 5 + [_i64] * 3 + [_int, _vp]),
     "mwc_ss_fwd_noalloc": (_int, [_vp] * 11 + [_i64] * 3 + [_int, _vp]),
+    "mwc_ss_fwd_ex_workspace_bytes": (_i64, [_i64, _i64, _i64, _int]),
+    "mwc_ss_fwd_ex": (_int, [_vp] * 8 + [_int] + [_vp] * 6 + [_i64] * 4 + [_int, _vp]),
+    "mwc_ss_bwd_ex_workspace_bytes": (_i64, [_i64, _i64, _i64, _int]),
+    "mwc_ss_bwd_ex": (_int, [_vp] * 8 + [_int] + [_vp] * 15 + [_i64] * 4 + [_int, _vp]),
     "mwc_check_last_launch": (_int, [_vp]),
     "mwc_selftest_wait_timeout": (_int, [_vp, _vp]),
 }

@@ -175,6 +175,76 @@ def ss_backward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev, dout, dh_last, ckpt,
     return du, ddelta, dA, dB, dC, dD, dh_prev
 
 
+def ss_forward_ex(u, delta, A, B_ssm, C_ssm, D_ssm, z=None, delta_bias=None,
+                  delta_softplus=False, h_prev=None, *, want_h_last=False, want_ckpt=False):
+    """Forward scan with the delta transform (bias, softplus) and the z gate
+    (mwc_ss_fwd_ex). Returns (out, out_z, h_last, ckpt): out is the ungated scan output,
+    out_z = out * silu(z) when z is given (else None)."""
+    Bb, L, D = u.shape
+    dev = u.device
+    out = torch.empty_like(u)
+    out_z = torch.empty_like(u) if z is not None else None
+    h_last = torch.empty((Bb, D, NSTATE), dtype=u.dtype, device=dev) if want_h_last else None
+    ckpt = (torch.empty((Bb, ckpt_count(L), D, NSTATE), dtype=torch.float32, device=dev)
+            if want_ckpt else None)
+    if L == 0 or Bb == 0 or D == 0:
+        if h_last is not None:
+            h_last.copy_(h_prev) if h_prev is not None else h_last.zero_()
+        return out, out_z, h_last, ckpt
+    lib = _lib.load()
+    dt = dtype_code(u)
+    with torch.cuda.device(dev):
+        ws_bytes = int(lib.mwc_ss_fwd_ex_workspace_bytes(Bb, L, D, dt))
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes > 0 else None
+        rc = lib.mwc_ss_fwd_ex(_p(u), _p(delta), _p(A), _p(B_ssm), _p(C_ssm), _p(D_ssm), _p(z),
+                               _p(delta_bias), int(bool(delta_softplus)), _p(h_prev), _p(out),
+                               _p(out_z), _p(h_last), _p(ckpt), _p(ws), ws_bytes, Bb, L, D, dt,
+                               _stream(dev))
+    _lib.check(rc, "selective_scan forward (extended)")
+    _check_waits(lib, dev, "selective_scan forward (extended)")
+    return out, out_z, h_last, ckpt
+
+
+def ss_backward_ex(u, delta, A, B_ssm, C_ssm, D_ssm, z, delta_bias, delta_softplus, h_prev,
+                   out, dout, dh_last, ckpt, want_dbias=False, want_dh_prev=False):
+    """Reverse scan with the delta transform and the z gate (mwc_ss_bwd_ex). dout is the
+    gradient of out_z when z is given, else of out. Returns
+    (du, ddelta, dA, dB, dC, dD, ddelta_bias, dz, dh_prev); unrequested entries are None."""
+    Bb, L, D = u.shape
+    dev = u.device
+    if dout is None:
+        dout = torch.zeros_like(u)
+    du = torch.empty_like(u)
+    ddelta = torch.empty_like(delta)
+    dA = torch.empty_like(A)
+    dB = torch.empty_like(B_ssm)
+    dC = torch.empty_like(C_ssm)
+    dD = torch.empty_like(D_ssm)
+    dbias = torch.empty(D, dtype=u.dtype, device=dev) if want_dbias else None
+    dz = torch.empty_like(u) if z is not None else None
+    dh_prev = torch.empty((Bb, D, NSTATE), dtype=u.dtype, device=dev) if want_dh_prev else None
+    if L == 0 or Bb == 0 or D == 0:
+        for t in (du, ddelta, dA, dB, dC, dD, dbias, dz):
+            if t is not None:
+                t.zero_()
+        if dh_prev is not None:
+            dh_prev.copy_(dh_last) if dh_last is not None else dh_prev.zero_()
+        return du, ddelta, dA, dB, dC, dD, dbias, dz, dh_prev
+    lib = _lib.load()
+    dt = dtype_code(u)
+    with torch.cuda.device(dev):
+        ws_bytes = int(lib.mwc_ss_bwd_ex_workspace_bytes(Bb, L, D, dt))
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        rc = lib.mwc_ss_bwd_ex(_p(u), _p(delta), _p(A), _p(B_ssm), _p(C_ssm), _p(D_ssm), _p(z),
+                               _p(delta_bias), int(bool(delta_softplus)), _p(h_prev), _p(out),
+                               _p(dout), _p(dh_last), _p(ckpt), _p(du), _p(ddelta), _p(dA),
+                               _p(dB), _p(dC), _p(dD), _p(dbias), _p(dz), _p(dh_prev), _p(ws),
+                               ws_bytes, Bb, L, D, dt, _stream(dev))
+    _lib.check(rc, "selective_scan backward (extended)")
+    _check_waits(lib, dev, "selective_scan backward (extended)")
+    return du, ddelta, dA, dB, dC, dD, dbias, dz, dh_prev
+
+
 def ss_fixup(delta, A, C_ssm, h_in, decay=None, out=None, h_last=None, ckpt=None):
     """Fold an incoming float32 state h_in (B, D, 16) into a scan run from zero, in place."""
     Bb, L, D = delta.shape
