@@ -45,6 +45,11 @@ CONFIGS = {
                             "float32 / float16)",
                    B=4, L=2048, D=5120, dtype=torch.bfloat16, mode="fwdbwd", dist="c3",
                    metric="selective-scan fwd+bwd GB/s, B=4 L=2048 D=5120 bf16"),
+    "c3ex": dict(workload="config 3 shape through selective_scan_fn with Mamba's block transforms "
+                          "(delta bias + softplus, z gate; an addition: the reference has neither)",
+                 B=4, L=2048, D=5120, dtype=torch.float16, mode="fwdbwd", dist="c3", block=True,
+                 metric="selective-scan block op fwd+bwd GB/s (softplus(delta+bias), y*silu(z)), "
+                        "B=4 L=2048 D=5120 fp16"),
     "c1": dict(workload="config 1: selective scan fwd+bwd fp32 B1 L1024 D256",
                B=1, L=1024, D=256, dtype=torch.float32, mode="fwdbwd", dist="c1",
                metric="selective-scan fwd+bwd GB/s, B=1 L=1024 D=256 fp32"),
@@ -292,8 +297,20 @@ def bench_fwdbwd(args, cfg, dev, world, rank, peaks):
     B, L, D = cfg["B"], cfg["L"], cfg["D"]
     ins, gy = make_ss_inputs(cfg, dev, seed=1000 + rank)
     es = ins[0].element_size()
+    block = cfg.get("block", False)
+    if block:
+        # block form: delta is the pre-activation, plus z (B, L, D) and delta_bias (D)
+        from mamba_windows_cuda.selective_scan_interface import selective_scan_fn
+        gen = torch.Generator(device=dev).manual_seed(2000 + rank)
+        ins[1] = (torch.randn(B, L, D, generator=gen, device=dev) * 0.5 - 1.0).to(cfg["dtype"])
+        ins = ins + [torch.randn(B, L, D, generator=gen, device=dev).to(cfg["dtype"]),
+                     (torch.randn(D, generator=gen, device=dev) * 0.3).to(cfg["dtype"])]
+
+        def mod(*a):
+            return selective_scan_fn(*a[:6], z=a[6], delta_bias=a[7], delta_softplus=True)
+    else:
+        mod = mwc.SelectiveScanCuda()
     leaves = [t.clone().requires_grad_(True) for t in ins]
-    mod = mwc.SelectiveScanCuda()
     stream = torch.cuda.current_stream(dev)
 
     def step(ev=None):
@@ -325,8 +342,16 @@ def bench_fwdbwd(args, cfg, dev, world, rank, peaks):
     bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
     ms_max = max_over_ranks(ms, world, dev)
     nbytes = ss_bytes(B, L, D, es, "fwdbwd")
+    if block:   # + z read and out_z written (fwd); z, ungated out read and dz written (bwd)
+        nbytes += 5 * B * L * D * es + 2 * D * es
     value = nbytes * world / (ms_max / args.steps / 1e3) / 1e9
-    launches_per_step = 3 if int(mwc._lib.load().mwc_ss_fwd_workspace_bytes(B, L, D, 1 if es == 2 else 0)) == 0 else 4
+    # our kernels per step: the forward scan (+ its carry fixup on the segmented path), the
+    # backward scan + its finalize; the block form adds the delta transform and the gate in
+    # both directions and the ddelta / dbias pair
+    nch = B * ((D + 127) // 128)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    seg_fwd = nch < sms and int(mwc._lib.load().mwc_ss_fwd_workspace_bytes(B, L, D, 0 if es == 4 else 1)) > 0
+    launches_per_step = (2 if seg_fwd else 1) + 2 + (6 if block else 0)
 
     # roofline of the dominant kernel (the backward: reverse scan + its fixed-order reduction)
     mufu_peak = 148 * 16 * peaks["sm_max_mhz"] * 1e6  # ex2 / s at the max SM clock

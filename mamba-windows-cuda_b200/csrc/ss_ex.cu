@@ -25,7 +25,7 @@ __device__ __forceinline__ float softplus_f(float x) { return x <= 20.f ? log1pf
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
 
 constexpr int EX_THREADS = 256;
-constexpr int EX_ROWS_PER_CHUNK = 256;   // rows of B*L summed per dbias partial
+constexpr int EX_ROWS_PER_CHUNK = 64;    // rows of B*L summed per dbias partial
 
 static unsigned ex_blocks(int64_t n) {
     return (unsigned)std::max<int64_t>(1, std::min<int64_t>((n + EX_THREADS - 1) / EX_THREADS, 148 * 16));
@@ -84,46 +84,201 @@ __global__ void ddelta_kernel(T* __restrict__ ddelta, const T* __restrict__ delt
     if (partial != nullptr) partial[chunk * D + d] = acc;
 }
 
+// dbias[d] = sum over chunks of partial[chunk][d]. Block = 32 channels x 8 lanes: lane j
+// sums chunks j, j + 8, ... in order, then the 8 sums are added in lane order (fixed order,
+// so the result is reproducible).
+constexpr int EX_FINAL_SPLIT = 8;
 template <typename T>
 __global__ void dbias_final_kernel(const float* __restrict__ partial, int64_t nchunk, int64_t D, T* __restrict__ dbias) {
-    for (int64_t d = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; d < D; d += (int64_t)gridDim.x * blockDim.x) {
-        float s = 0.f;
-        for (int64_t c = 0; c < nchunk; ++c) s += partial[c * D + d];
-        dbias[d] = from_f<T>(s);
+    __shared__ float part[EX_FINAL_SPLIT][32];
+    const int c = threadIdx.x & 31, j = threadIdx.x >> 5;
+    const int64_t d = (int64_t)blockIdx.x * 32 + c;
+    float sum = 0.f;
+    if (d < D)
+        for (int64_t k = j; k < nchunk; k += EX_FINAL_SPLIT) sum += partial[k * D + d];
+    part[j][c] = sum;
+    __syncthreads();
+    if (j == 0 && d < D) {
+        float t = part[0][c];
+#pragma unroll
+        for (int q = 1; q < EX_FINAL_SPLIT; ++q) t += part[q][c];
+        dbias[d] = from_f<T>(t);
+    }
+}
+
+// ---- 16-byte vector forms (8 half / bf16 or 4 float elements per thread step) ----
+template <typename T>
+struct VecT {
+    static constexpr int N = 16 / (int)sizeof(T);
+};
+
+template <typename T>
+__device__ __forceinline__ void ld_vec(const T* p, float (&v)[VecT<T>::N]) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(p);
+    const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int k = 0; k < VecT<T>::N; ++k) v[k] = to_f(e[k]);
+}
+
+template <typename T>
+__device__ __forceinline__ void st_vec(T* p, const float (&v)[VecT<T>::N]) {
+    uint4 raw;
+    T* e = reinterpret_cast<T*>(&raw);
+#pragma unroll
+    for (int k = 0; k < VecT<T>::N; ++k) e[k] = from_f<T>(v[k]);
+    *reinterpret_cast<uint4*>(p) = raw;
+}
+
+template <typename T>
+__global__ void delta_eff_vec_kernel(const T* __restrict__ delta, const T* __restrict__ bias, int softplus,
+                                     T* __restrict__ out, int64_t nv, int64_t D) {
+    constexpr int N = VecT<T>::N;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
+        float v[N], b[N];
+        ld_vec<T>(delta + i * N, v);
+        if (bias != nullptr) ld_vec<T>(bias + (i * N) % D, b);
+#pragma unroll
+        for (int k = 0; k < N; ++k) {
+            const float x = v[k] + (bias != nullptr ? b[k] : 0.f);
+            v[k] = softplus ? softplus_f(x) : x;
+        }
+        st_vec<T>(out + i * N, v);
+    }
+}
+
+template <typename T>
+__global__ void gate_fwd_vec_kernel(const T* __restrict__ y, const T* __restrict__ z, T* __restrict__ out_z,
+                                    int64_t nv) {
+    constexpr int N = VecT<T>::N;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
+        float yv[N], zv[N];
+        ld_vec<T>(y + i * N, yv);
+        ld_vec<T>(z + i * N, zv);
+#pragma unroll
+        for (int k = 0; k < N; ++k) yv[k] = yv[k] * zv[k] * sigmoid_f(zv[k]);
+        st_vec<T>(out_z + i * N, yv);
+    }
+}
+
+template <typename T>
+__global__ void gate_bwd_vec_kernel(const T* __restrict__ dout, const T* __restrict__ z, const T* __restrict__ y,
+                                    T* __restrict__ gy, T* __restrict__ dz, int64_t nv) {
+    constexpr int N = VecT<T>::N;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
+        float g[N], zv[N], yv[N], a[N], b[N];
+        ld_vec<T>(dout + i * N, g);
+        ld_vec<T>(z + i * N, zv);
+        ld_vec<T>(y + i * N, yv);
+#pragma unroll
+        for (int k = 0; k < N; ++k) {
+            const float sg = sigmoid_f(zv[k]);
+            a[k] = g[k] * zv[k] * sg;
+            b[k] = g[k] * yv[k] * sg * (1.f + zv[k] * (1.f - sg));
+        }
+        st_vec<T>(gy + i * N, a);
+        st_vec<T>(dz + i * N, b);
+    }
+}
+
+// thread = one 16-byte group of channels for a chunk of rows (rows in order)
+template <typename T>
+__global__ void ddelta_vec_kernel(T* __restrict__ ddelta, const T* __restrict__ delta, const T* __restrict__ bias,
+                                  int softplus, float* __restrict__ partial, int64_t rows, int64_t D) {
+    constexpr int N = VecT<T>::N;
+    const int64_t dv = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (dv * N >= D) return;
+    const int64_t d0 = dv * N;
+    const int64_t chunk = blockIdx.y;
+    float bd[N];
+    if (bias != nullptr) ld_vec<T>(bias + d0, bd);
+    else {
+#pragma unroll
+        for (int k = 0; k < N; ++k) bd[k] = 0.f;
+    }
+    const int64_t r0 = chunk * EX_ROWS_PER_CHUNK;
+    const int64_t r1 = rows < r0 + EX_ROWS_PER_CHUNK ? rows : r0 + EX_ROWS_PER_CHUNK;
+    float acc[N];
+#pragma unroll
+    for (int k = 0; k < N; ++k) acc[k] = 0.f;
+    for (int64_t r = r0; r < r1; ++r) {
+        float g[N];
+        ld_vec<T>(ddelta + r * D + d0, g);
+        if (softplus) {
+            float x[N];
+            ld_vec<T>(delta + r * D + d0, x);
+#pragma unroll
+            for (int k = 0; k < N; ++k) g[k] *= sigmoid_f(x[k] + bd[k]);
+            st_vec<T>(ddelta + r * D + d0, g);
+        }
+#pragma unroll
+        for (int k = 0; k < N; ++k) acc[k] += g[k];
+    }
+    if (partial != nullptr) {
+#pragma unroll
+        for (int k = 0; k < N; ++k) partial[chunk * D + d0 + k] = acc[k];
     }
 }
 
 template <typename T>
 static cudaError_t launch_delta_eff(const void* delta, const void* bias, int softplus, void* out, int64_t n,
                                     int64_t D, cudaStream_t s) {
-    delta_eff_kernel<T><<<ex_blocks(n), EX_THREADS, 0, s>>>(static_cast<const T*>(delta), static_cast<const T*>(bias),
-                                                            softplus, static_cast<T*>(out), n, D);
+    constexpr int N = VecT<T>::N;
+    if (D % N == 0) {
+        delta_eff_vec_kernel<T><<<ex_blocks(n / N), EX_THREADS, 0, s>>>(
+            static_cast<const T*>(delta), static_cast<const T*>(bias), softplus, static_cast<T*>(out), n / N, D);
+    } else {
+        delta_eff_kernel<T><<<ex_blocks(n), EX_THREADS, 0, s>>>(static_cast<const T*>(delta), static_cast<const T*>(bias),
+                                                                softplus, static_cast<T*>(out), n, D);
+    }
     return cudaGetLastError();
 }
 template <typename T>
 static cudaError_t launch_gate_fwd(const void* y, const void* z, void* out_z, int64_t n, cudaStream_t s) {
-    gate_fwd_kernel<T><<<ex_blocks(n), EX_THREADS, 0, s>>>(static_cast<const T*>(y), static_cast<const T*>(z),
-                                                           static_cast<T*>(out_z), n);
+    constexpr int N = VecT<T>::N;
+    if (n % N == 0) {
+        gate_fwd_vec_kernel<T><<<ex_blocks(n / N), EX_THREADS, 0, s>>>(
+            static_cast<const T*>(y), static_cast<const T*>(z), static_cast<T*>(out_z), n / N);
+    } else {
+        gate_fwd_kernel<T><<<ex_blocks(n), EX_THREADS, 0, s>>>(static_cast<const T*>(y), static_cast<const T*>(z),
+                                                               static_cast<T*>(out_z), n);
+    }
     return cudaGetLastError();
 }
 template <typename T>
 static cudaError_t launch_gate_bwd(const void* dout, const void* z, const void* y, void* gy, void* dz, int64_t n,
                                    cudaStream_t s) {
-    gate_bwd_kernel<T><<<ex_blocks(n), EX_THREADS, 0, s>>>(static_cast<const T*>(dout), static_cast<const T*>(z),
-                                                           static_cast<const T*>(y), static_cast<T*>(gy),
-                                                           static_cast<T*>(dz), n);
+    constexpr int N = VecT<T>::N;
+    if (n % N == 0) {
+        gate_bwd_vec_kernel<T><<<ex_blocks(n / N), EX_THREADS, 0, s>>>(
+            static_cast<const T*>(dout), static_cast<const T*>(z), static_cast<const T*>(y), static_cast<T*>(gy),
+            static_cast<T*>(dz), n / N);
+    } else {
+        gate_bwd_kernel<T><<<ex_blocks(n), EX_THREADS, 0, s>>>(static_cast<const T*>(dout), static_cast<const T*>(z),
+                                                               static_cast<const T*>(y), static_cast<T*>(gy),
+                                                               static_cast<T*>(dz), n);
+    }
     return cudaGetLastError();
 }
 template <typename T>
 static cudaError_t launch_ddelta(void* ddelta, const void* delta, const void* bias, int softplus, float* partial,
                                  int64_t rows, int64_t D, void* dbias, cudaStream_t s) {
     const int64_t nchunk = (rows + EX_ROWS_PER_CHUNK - 1) / EX_ROWS_PER_CHUNK;
-    dim3 grid((unsigned)((D + EX_THREADS - 1) / EX_THREADS), (unsigned)nchunk);
-    ddelta_kernel<T><<<grid, EX_THREADS, 0, s>>>(static_cast<T*>(ddelta), static_cast<const T*>(delta),
-                                                 static_cast<const T*>(bias), softplus, partial, rows, D);
+    constexpr int N = VecT<T>::N;
+    if (D % N == 0) {
+        const int64_t groups = D / N;
+        const int tpb = (int)std::min<int64_t>(EX_THREADS, ((groups + 31) / 32) * 32);
+        dim3 grid((unsigned)((groups + tpb - 1) / tpb), (unsigned)nchunk);
+        ddelta_vec_kernel<T><<<grid, tpb, 0, s>>>(static_cast<T*>(ddelta), static_cast<const T*>(delta),
+                                                  static_cast<const T*>(bias), softplus, partial, rows, D);
+    } else {
+        dim3 grid((unsigned)((D + EX_THREADS - 1) / EX_THREADS), (unsigned)nchunk);
+        ddelta_kernel<T><<<grid, EX_THREADS, 0, s>>>(static_cast<T*>(ddelta), static_cast<const T*>(delta),
+                                                     static_cast<const T*>(bias), softplus, partial, rows, D);
+    }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess || dbias == nullptr) return e;
-    dbias_final_kernel<T><<<ex_blocks(D), EX_THREADS, 0, s>>>(partial, nchunk, D, static_cast<T*>(dbias));
+    dbias_final_kernel<T><<<(unsigned)((D + 31) / 32), 32 * EX_FINAL_SPLIT, 0, s>>>(partial, nchunk, D,
+                                                                                   static_cast<T*>(dbias));
     return cudaGetLastError();
 }
 
