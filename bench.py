@@ -54,13 +54,16 @@ CONFIGS = {
                B=1, L=1024, D=256, dtype=torch.float32, mode="fwdbwd", dist="c1",
                metric="selective-scan fwd+bwd GB/s, B=1 L=1024 D=256 fp32"),
     "c2": dict(workload="config 2: Mamba-1.4B-like inference forward_with_state fp16",
-               B=8, L=2048, D=4096, dtype=torch.float16, mode="fwd", dist="c2"),
+               B=8, L=2048, D=4096, dtype=torch.float16, mode="fwd", dist="c2",
+               metric="selective-scan inference forward_with_state GB/s, B=8 L=2048 D=4096 fp16"),
     "c4": dict(workload="config 4: streaming scan fp32, 16 chunks of 65536 with h_prev/h_last "
                         "(2^20 tokens; sequence-sharded across ranks for N > 1)",
                B=1, L=65536, D=2048, dtype=torch.float32, mode="stream", dist="c4", chunks=16,
                metric="selective-scan streaming forward GB/s, B=1 L=2^20 (16 x 65536) D=2048 fp32"),
-    "c5": dict(workload="config 5: parallel_scan_fn fp32 (16, 1024, 16384, 1)",
-               B=16, L=16384, D=1024, dtype=torch.float32, mode="pscan", dist="c5"),
+    "c5": dict(workload="config 5: parallel_scan_fn fp32 (B=16, D=1024, L=16384, 1), a~U(0.9,1), "
+                        "b~N(0,1)",
+               B=16, L=16384, D=1024, dtype=torch.float32, mode="pscan", dist="c5",
+               metric="parallel_scan_fn GB/s, (16, 1024, 16384, 1) fp32"),
 }
 
 
@@ -242,6 +245,13 @@ def oracle_sample(cfg, target_s, seed=0):
     es = torch.tensor([], dtype=cfg["dtype"]).element_size()
 
     def run(Ls):
+        if cfg["mode"] == "pscan":   # linear recurrence along L of (B, D, L, 1)
+            g = torch.Generator().manual_seed(seed)
+            a = (torch.rand(B, D, Ls, 1, generator=g) * 0.1 + 0.9).double().numpy()
+            x = torch.randn(B, D, Ls, 1, generator=g).double().numpy()
+            t0 = time.perf_counter()
+            O.lin_fwd(a, x)
+            return time.perf_counter() - t0
         (u, delta, A, Bm, Cm, Dv), gy = make_ss_inputs(cfg, "cpu", seed, L=Ls)
         n = [t.double().numpy() for t in (u, delta, A, Bm, Cm, Dv)]
         t0 = time.perf_counter()
@@ -254,9 +264,13 @@ def oracle_sample(cfg, target_s, seed=0):
     t = run(probe)
     Ls = int(min(cfg["L"], max(16, probe * target_s / max(t, 1e-6))))
     secs = run(Ls)
-    nbytes = ss_bytes(B, Ls, D, es, cfg["mode"])
-    desc = (f"B={B} L={Ls} (of {cfg['L']}) D={D} slice, float64 oracle on "
-            f"{'fp16-valued' if es == 2 else 'fp32'} inputs, fwd{'+bwd' if cfg['mode'] == 'fwdbwd' else ''}")
+    if cfg["mode"] == "pscan":
+        nbytes = 12 * B * D * Ls
+        desc = f"B={B} D={D} L={Ls} (of {cfg['L']}) slice, float64 oracle linear recurrence"
+    else:
+        nbytes = ss_bytes(B, Ls, D, es, cfg["mode"])
+        desc = (f"B={B} L={Ls} (of {cfg['L']}) D={D} slice, float64 oracle on "
+                f"{'fp16-valued' if es == 2 else 'fp32'} inputs, fwd{'+bwd' if cfg['mode'] == 'fwdbwd' else ''}")
     return secs, nbytes, desc, O.num_threads()
 
 
@@ -510,6 +524,114 @@ def emit(line):
         os.write(_JSON_FD, data)
 
 
+def _timed(args, world, dev, fn):
+    """Warm-up, then K timed calls bracketed by events on the current stream; returns the
+    max-over-ranks milliseconds of the K calls and the clock summary."""
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        fn()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier_sync(world, dev)
+    with ClockSampler(dev.index if dev.index is not None else 0) as clk:
+        start.record(stream)
+        for _ in range(args.steps):
+            fn()
+        stop.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier_sync(world, dev)
+    return max_over_ranks(start.elapsed_time(stop), world, dev), clk.summary()
+
+
+def _e2e(args, world, dev, host_in, host_out, fn_dev, nbytes):
+    """Same op through host buffers: H2D of the step's inputs, the op, D2H of its outputs,
+    all inside the timed region."""
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        outs = fn_dev([h.to(dev, non_blocking=True) for h in host_in])
+        for ho, o in zip(host_out, outs):
+            ho.copy_(o, non_blocking=True)
+
+    steps = max(3, min(args.steps, 10))
+    for _ in range(2):
+        step()
+    barrier_sync(world, dev)
+    s2, t2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record(stream)
+    for _ in range(steps):
+        step()
+    t2.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = max_over_ranks(s2.elapsed_time(t2), world, dev) / steps
+    return {"value": nbytes * world / (ms / 1e3) / 1e9, "unit": "GB/s",
+            "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in host_in),
+            "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in host_out), "ms_per_step": ms}
+
+
+def bench_fwd(args, cfg, dev, world, rank, peaks):
+    """Config 2: inference forward_with_state (h0 = 0, returns out and h_last), fp16; each
+    rank its own batch (batch x D tiles at N GPUs, no exchange)."""
+    import mamba_windows_cuda as mwc
+    B, L, D = cfg["B"], cfg["L"], cfg["D"]
+    ins, _ = make_ss_inputs(cfg, dev, seed=4000 + rank)
+    es = ins[0].element_size()
+    mod = mwc.SelectiveScanCuda()
+
+    def op(xs):
+        with torch.no_grad():
+            return mod.forward_with_state(*xs)
+
+    ms, clk = _timed(args, world, dev, lambda: op(ins))
+    nbytes = ss_bytes(B, L, D, es, "fwd")
+    t = ms / args.steps / 1e3
+    mufu_peak = 148 * 16 * peaks["sm_max_mhz"] * 1e6
+    ex2 = 16 * B * L * D
+    roofline = {"kernel": "ss_fwd_persistent_kernel (forward, h_last out)", "bound": "mufu",
+                "achieved": ex2 / t / 1e9, "peak": mufu_peak / 1e9, "unit": "Gex2/s",
+                "frac": ex2 / t / mufu_peak, "traffic": None,
+                "hbm": {"achieved": nbytes / t / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                        "frac": nbytes / t / 1e9 / peaks["hbm_gbs"], "peak_source": peaks["source"]},
+                "model": "max(algorithmic bytes / HBM, 16 ex2 per element / MUFU)"}
+    host_in = [x.cpu().pin_memory() for x in ins]
+    host_out = [torch.empty(ins[0].shape, dtype=ins[0].dtype).pin_memory(),
+                torch.empty((B, D, NSTATE), dtype=ins[0].dtype).pin_memory()]
+    e2e = _e2e(args, world, dev, host_in, host_out, op, nbytes)
+    return dict(value=nbytes * world / t / 1e9, ms_per_step=ms / args.steps, roofline=roofline,
+                e2e=e2e, clocks=clk, gpu_launches=1 * args.steps, dtype="f32",
+                io_dtype=str(cfg["dtype"]).replace("torch.", ""),
+                parallelism=f"batch tiles x{world}: one independent batch per rank, no collective")
+
+
+def bench_pscan(args, cfg, dev, world, rank, peaks):
+    """Config 5: parallel_scan_fn, H_t = A_t H_{t-1} + X_t along L of (B, D, L, 1), fp32;
+    HBM-bound (read A, X, write H: 12 bytes per element)."""
+    from mamba_windows_cuda import parallel_scan_fn
+    B, L, D = cfg["B"], cfg["L"], cfg["D"]
+    gen = torch.Generator(device=dev).manual_seed(5000 + rank)
+    A = torch.rand(B, D, L, 1, generator=gen, device=dev) * 0.1 + 0.9
+    X = torch.randn(B, D, L, 1, generator=gen, device=dev)
+
+    def op(xs):
+        with torch.no_grad():
+            return (parallel_scan_fn(*xs),)
+
+    ms, clk = _timed(args, world, dev, lambda: op((A, X)))
+    E = B * D * L
+    nbytes = 12 * E
+    t = ms / args.steps / 1e3
+    roofline = {"kernel": "lin_fwd_kernel (warp-shuffle scan of affine maps)", "bound": "hbm",
+                "achieved": nbytes / t / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": nbytes / t / 1e9 / peaks["hbm_gbs"], "traffic": None,
+                "peak_source": peaks["source"], "model": "12 bytes per element (A, X read; H written)"}
+    host_in = [A.cpu().pin_memory(), X.cpu().pin_memory()]
+    host_out = [torch.empty(A.shape, dtype=A.dtype).pin_memory()]
+    e2e = _e2e(args, world, dev, host_in, host_out, op, nbytes)
+    return dict(value=nbytes * world / t / 1e9, ms_per_step=ms / args.steps, roofline=roofline,
+                e2e=e2e, clocks=clk, gpu_launches=1 * args.steps, dtype="f32", io_dtype="float32",
+                l2=f"{nbytes / 1e9:.1f} GB per step, far above the 126 MB L2; no flush",
+                parallelism=f"replicas x{world}: one independent scan per rank, no collective")
+
+
 def main():
     global _JSON_FD
     # Keep stdout for the JSON line alone: libraries that print banners to fd 1 (NCCL's
@@ -542,6 +664,10 @@ def main():
     torch.cuda.set_device(dev)
     if cfg["mode"] == "stream":
         res = bench_stream(args, cfg, dev, world, rank, peaks)
+    elif cfg["mode"] == "fwd":
+        res = bench_fwd(args, cfg, dev, world, rank, peaks)
+    elif cfg["mode"] == "pscan":
+        res = bench_pscan(args, cfg, dev, world, rank, peaks)
     elif cfg["mode"] == "fwdbwd":
         res = bench_fwdbwd(args, cfg, dev, world, rank, peaks)
     else:
