@@ -50,6 +50,10 @@ CONFIGS = {
                  B=4, L=2048, D=5120, dtype=torch.float16, mode="fwdbwd", dist="c3", block=True,
                  metric="selective-scan block op fwd+bwd GB/s (softplus(delta+bias), y*silu(z)), "
                         "B=4 L=2048 D=5120 fp16"),
+    "conv": dict(workload="causal conv1d producer of u (width 4, SiLU) at the config-3 shape, fwd+bwd "
+                          "(an addition: the reference has no conv1d)",
+                 B=4, L=2048, D=5120, dtype=torch.float16, mode="conv", dist="c3",
+                 metric="causal_conv1d fwd+bwd GB/s, (4, 2048, 5120) width 4 SiLU fp16"),
     "c1": dict(workload="config 1: selective scan fwd+bwd fp32 B1 L1024 D256",
                B=1, L=1024, D=256, dtype=torch.float32, mode="fwdbwd", dist="c1",
                metric="selective-scan fwd+bwd GB/s, B=1 L=1024 D=256 fp32"),
@@ -632,6 +636,75 @@ def bench_pscan(args, cfg, dev, world, rank, peaks):
                 parallelism=f"replicas x{world}: one independent scan per rank, no collective")
 
 
+def bench_conv(args, cfg, dev, world, rank, peaks):
+    """Causal conv1d (width 4, SiLU) forward + backward: HBM-bound (x read, y written;
+    x, dy read, dx written: 10 bytes per fp16 element, plus the weight / bias partials).
+    Roofline: the backward op (TMA-staged kernel + fixed-order weight reduction, the larger
+    share of the step), timed per step with events on the launching stream."""
+    from mamba_windows_cuda.causal_conv1d import causal_conv1d_fn
+    B, L, D = cfg["B"], cfg["L"], cfg["D"]
+    gen = torch.Generator(device=dev).manual_seed(6000 + rank)
+    dt = cfg["dtype"]
+    x = torch.randn(B, L, D, generator=gen, device=dev).to(dt).requires_grad_(True)
+    w = (torch.randn(D, 4, generator=gen, device=dev) * 0.5).to(dt).requires_grad_(True)
+    b = (torch.randn(D, generator=gen, device=dev) * 0.1).to(dt).requires_grad_(True)
+    dy = torch.randn(B, L, D, generator=gen, device=dev).to(dt)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(ev=None):
+        for t in (x, w, b):
+            t.grad = None
+        if ev is not None:
+            ev[0].record(stream)
+        y = causal_conv1d_fn(x, w, b, "silu")
+        if ev is not None:
+            ev[1].record(stream)
+        y.backward(dy)
+        if ev is not None:
+            ev[2].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier_sync(world, dev)
+    with ClockSampler(dev.index if dev.index is not None else 0) as clk:
+        start.record(stream)
+        for i in range(args.steps):
+            step(evs[i])
+        stop.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier_sync(world, dev)
+    ms = max_over_ranks(start.elapsed_time(stop), world, dev)
+    fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    es = x.element_size()
+    E = B * L * D
+    nbytes = 10 * E * es // 2
+    bwd_bytes = 3 * E * es + 4 * D * es * 2   # x, dy read, dx written; weights in, dweight out
+    t = ms / args.steps / 1e3
+    achieved = bwd_bytes / (bwd_ms / 1e3) / 1e9
+    roofline = {"kernel": "conv1d_bwd_tma_kernel + conv1d_reduce_kernel (backward op)",
+                "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"], "traffic": None, "peak_source": peaks["source"],
+                "model": "x, dy read + dx written (3 x 2 B per fp16 element)",
+                "per_op_ms": {"fwd": fwd_ms, "bwd": bwd_ms},
+                "fwd_frac": 2 * E * es / (fwd_ms / 1e3) / 1e9 / peaks["hbm_gbs"]}
+    xh, dyh = x.detach().cpu().pin_memory(), dy.cpu().pin_memory()
+    dxh = torch.empty(x.shape, dtype=dt).pin_memory()
+
+    def op(xs):
+        xi = xs[0].requires_grad_(True)
+        causal_conv1d_fn(xi, w, b, "silu").backward(xs[1])
+        return (xi.grad,)
+
+    e2e = _e2e(args, world, dev, [xh, dyh], [dxh], op, nbytes)
+    return dict(value=nbytes * world / t / 1e9, ms_per_step=ms / args.steps, roofline=roofline, e2e=e2e,
+                clocks=clk.summary(), gpu_launches=3 * args.steps, dtype="f32",
+                io_dtype=str(dt).replace("torch.", ""),
+                parallelism=f"replicas x{world}: one independent batch per rank, no collective")
+
+
 def main():
     global _JSON_FD
     # Keep stdout for the JSON line alone: libraries that print banners to fd 1 (NCCL's
@@ -668,6 +741,8 @@ def main():
         res = bench_fwd(args, cfg, dev, world, rank, peaks)
     elif cfg["mode"] == "pscan":
         res = bench_pscan(args, cfg, dev, world, rank, peaks)
+    elif cfg["mode"] == "conv":
+        res = bench_conv(args, cfg, dev, world, rank, peaks)
     elif cfg["mode"] == "fwdbwd":
         res = bench_fwdbwd(args, cfg, dev, world, rank, peaks)
     else:

@@ -175,6 +175,25 @@ MWC_API int mwc_ss_bwd_ex(const void* u, const void* delta, const void* A, const
                           void* stream);
 
 /*
+ * Causal depthwise conv1d, the producer of u in Mamba's block (not in the reference; the
+ * official Mamba stack ships it as causal_conv1d). Channel-last like the scan:
+ *   x, y, dy, dx (B, L, D); weight, dweight (D, W), 1 <= W <= 4; bias, dbias (D) or NULL;
+ *   x_prev, dx_prev (B, W-1, D) or NULL: the W-1 inputs before t = 0 (zero when NULL), for
+ *   chunked streaming; activation 0 = none, 1 = SiLU.
+ *   y[b,t,d] = act(bias[d] + sum_k weight[d,k] x[b, t-(W-1)+k, d])
+ * The backward recomputes the pre-activation from x; dweight / dbias are reduced in a fixed
+ * order (workspace: mwc_conv1d_bwd_workspace_bytes).
+ */
+MWC_API int mwc_conv1d_fwd(const void* x, const void* weight, const void* bias, const void* x_prev,
+                           int activation, void* y, int64_t B, int64_t L, int64_t D, int64_t W,
+                           int dtype, void* stream);
+MWC_API int64_t mwc_conv1d_bwd_workspace_bytes(int64_t B, int64_t L, int64_t D, int64_t W);
+MWC_API int mwc_conv1d_bwd(const void* x, const void* weight, const void* bias, const void* x_prev,
+                           int activation, const void* dy, void* dx, void* dweight, void* dbias,
+                           void* dx_prev, void* workspace, int64_t workspace_bytes, int64_t B,
+                           int64_t L, int64_t D, int64_t W, int dtype, void* stream);
+
+/*
  * mwc_check_last_launch -- waits for `stream` and reports whether the last persistent
  * forward / backward kernel launched from this thread gave up on a bounded device wait
  * (returns MWC_ERR_TIMEOUT, results of that call are invalid) or not (MWC_OK). The

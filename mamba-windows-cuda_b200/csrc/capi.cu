@@ -105,6 +105,7 @@ int report_error(int code, const char* msg) {
     return code;
 }
 int report_ok() { return ok(); }
+void note_err_word(const int* word) { g_last_err_word = word; }
 int current_device_sms() { return device_sms(); }
 }  // namespace mwc
 

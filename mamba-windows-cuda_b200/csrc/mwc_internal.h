@@ -162,6 +162,8 @@ cudaError_t launch_bwd_persistent(PBwdArgs& a, const PersistPlan& pl, int dtype,
 // Error reporting shared by the C entry points (capi.cu).
 int report_error(int code, const char* msg);
 int report_ok();
+// Error word that mwc_check_last_launch reads for the last launch on this thread (nullptr: none).
+void note_err_word(const int* word);
 int current_device_sms();
 
 // Launch-shape descriptors chosen by the host heuristics in capi.cu.

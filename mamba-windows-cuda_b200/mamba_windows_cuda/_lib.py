@@ -41,6 +41,9 @@ SIGNATURES = {
     "mwc_ss_fwd_ex": (_int, [_vp] * 8 + [_int] + [_vp] * 6 + [_i64] * 4 + [_int, _vp]),
     "mwc_ss_bwd_ex_workspace_bytes": (_i64, [_i64, _i64, _i64, _int]),
     "mwc_ss_bwd_ex": (_int, [_vp] * 8 + [_int] + [_vp] * 15 + [_i64] * 4 + [_int, _vp]),
+    "mwc_conv1d_fwd": (_int, [_vp] * 4 + [_int, _vp] + [_i64] * 4 + [_int, _vp]),
+    "mwc_conv1d_bwd_workspace_bytes": (_i64, [_i64] * 4),
+    "mwc_conv1d_bwd": (_int, [_vp] * 4 + [_int] + [_vp] * 6 + [_i64] * 5 + [_int, _vp]),
     "mwc_check_last_launch": (_int, [_vp]),
     "mwc_selftest_wait_timeout": (_int, [_vp, _vp]),
 }
