@@ -21,8 +21,12 @@
 
 namespace mwc {
 
-__device__ __forceinline__ float softplus_f(float x) { return x <= 20.f ? log1pf(expf(x)) : x; }
-__device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
+// softplus and the logistic function through the fast exp / log / divide intrinsics: these
+// kernels stream 4-10 bytes per element, and the precise log1pf / expf / IEEE division made
+// them compute-bound. Errors: softplus a few 1e-7 absolute (the log of 1 + e^x near 1),
+// sigmoid a few ulp; sigmoid is 0 below x = -87 and softplus is x above 20.
+__device__ __forceinline__ float softplus_f(float x) { return x <= 20.f ? __logf(1.f + __expf(x)) : x; }
+__device__ __forceinline__ float sigmoid_f(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
 
 constexpr int EX_THREADS = 256;
 constexpr int EX_ROWS_PER_CHUNK = 64;    // rows of B*L summed per dbias partial
@@ -133,10 +137,17 @@ template <typename T>
 __global__ void delta_eff_vec_kernel(const T* __restrict__ delta, const T* __restrict__ bias, int softplus,
                                      T* __restrict__ out, int64_t nv, int64_t D) {
     constexpr int N = VecT<T>::N;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    // channel of the vector, advanced by the grid stride without a division per step
+    const int64_t cstep = (stride * N) % D;
+    int64_t col = (i0 * N) % D;
+    for (int64_t i = i0; i < nv; i += stride) {
         float v[N], b[N];
         ld_vec<T>(delta + i * N, v);
-        if (bias != nullptr) ld_vec<T>(bias + (i * N) % D, b);
+        if (bias != nullptr) ld_vec<T>(bias + col, b);
+        col += cstep;
+        if (col >= D) col -= D;
 #pragma unroll
         for (int k = 0; k < N; ++k) {
             const float x = v[k] + (bias != nullptr ? b[k] : 0.f);
@@ -200,6 +211,7 @@ __global__ void ddelta_vec_kernel(T* __restrict__ ddelta, const T* __restrict__ 
     float acc[N];
 #pragma unroll
     for (int k = 0; k < N; ++k) acc[k] = 0.f;
+#pragma unroll 4
     for (int64_t r = r0; r < r1; ++r) {
         float g[N];
         ld_vec<T>(ddelta + r * D + d0, g);
