@@ -74,9 +74,12 @@ CONFIGS = {
 # DRAM bytes (read + write) of one launch of the dominant kernel, from one ncu capture of
 # this bench's own command (profiles/ss_fwd_bwd_persistent_c3_fp16.md).
 CAPTURED_TRAFFIC = {
-    "c3": {"bytes": 419.062784e6 + 205.661440e6,
+    "c3": {"bytes": 419.029248e6 + 204.617216e6,
            "source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, ss_bwd_persistent_kernel, "
                      "profiles/ss_fwd_bwd_persistent_c3_fp16.md"},
+    "conv": {"bytes": 167.935232e6 + 54.496256e6,
+             "source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, conv1d_bwd_tma_kernel (part of "
+                       "dx is still in L2 at kernel end), profiles/conv1d_tma_conv_fp16.md"},
 }
 
 
@@ -686,7 +689,10 @@ def bench_conv(args, cfg, dev, world, rank, peaks):
     achieved = bwd_bytes / (bwd_ms / 1e3) / 1e9
     roofline = {"kernel": "conv1d_bwd_tma_kernel + conv1d_reduce_kernel (backward op)",
                 "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / peaks["hbm_gbs"], "traffic": None, "peak_source": peaks["source"],
+                "frac": achieved / peaks["hbm_gbs"],
+                "traffic": CAPTURED_TRAFFIC["conv"]["bytes"] if args.config == "conv" else None,
+                "traffic_source": CAPTURED_TRAFFIC["conv"]["source"] if args.config == "conv" else None,
+                "peak_source": peaks["source"],
                 "model": "x, dy read + dx written (3 x 2 B per fp16 element)",
                 "per_op_ms": {"fwd": fwd_ms, "bwd": bwd_ms},
                 "fwd_frac": 2 * E * es / (fwd_ms / 1e3) / 1e9 / peaks["hbm_gbs"]}
