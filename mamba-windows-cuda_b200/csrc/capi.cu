@@ -127,7 +127,8 @@ int64_t mwc_ss_fwd_workspace_bytes(int64_t B, int64_t L, int64_t D, int dtype) {
     const int sms = device_sms();
     const FwdPlan plan = plan_fwd(B, L, D, dtype, sms);
     int64_t need = align_up(fwd_carry_floats(plan, B, D) * 4, 256);
-    const PersistPlan pp = plan_persistent(B, L, D, sms);
+    PersistPlan pp = plan_persistent(B, L, D, sms);
+    if (!pp.ok) pp = plan_persistent_split(B, L, D, sms);
     if (pp.ok) need = std::max<int64_t>(need, align_up(persistent_ws_bytes(pp), 256));
     return need;
 }
@@ -147,7 +148,11 @@ int mwc_ss_fwd(const void* u, const void* delta, const void* A, const void* Bm, 
     if (B == 0 || D == 0) return ok();
     const int sms = device_sms();
     const size_t es0 = elem_size(dtype);
-    const PersistPlan pp = plan_persistent(B, L, D, sms);
+    // many (batch, 128-channel) chains: chained segments; few chains: state-only pass, fold,
+    // seeded pass over independent L-segments
+    const PersistPlan pchain = plan_persistent(B, L, D, sms);
+    const bool split = !pchain.ok;
+    const PersistPlan pp = split ? plan_persistent_split(B, L, D, sms) : pchain;
     const bool tma_ok = pp.ok && ((D * (int64_t)es0) % 16 == 0) && aligned16(u) &&
                         aligned16(delta) && aligned16(Bm) && aligned16(Cm) && aligned16(A) &&
                         aligned16(Dv) && (!h_prev || aligned16(h_prev)) &&
@@ -171,8 +176,9 @@ int mwc_ss_fwd(const void* u, const void* delta, const void* A, const void* Bm, 
             pa.B = (int)B; pa.L = (int)L; pa.D = (int)D;
             pa.nck = (int)mwc_ss_ckpt_count(L);
             pa.has_out = out != nullptr;
-            cudaError_t e = launch_fwd_persistent(pa, pp, dtype, workspace,
-                                                  static_cast<cudaStream_t>(stream));
+            cudaStream_t st = static_cast<cudaStream_t>(stream);
+            cudaError_t e = split ? launch_fwd_persistent_split(pa, pp, dtype, workspace, st)
+                                  : launch_fwd_persistent(pa, pp, dtype, workspace, st);
             if (e != cudaSuccess) return cuda_fail(e, "selective-scan persistent forward launch");
             g_last_err_word = pa.err;
             return ok();

@@ -114,6 +114,12 @@ struct PFwdArgs {
     int B, L, D;
     int nblk, nchains, K, seg_tiles, ntiles, nck;
     int has_out;
+    // 0: chained segments (segment k waits for the record segment k-1 publishes);
+    // 1: state only: segments 0..K-2 scan independently (segment 0 from h_prev, the others
+    //    from zero) and each writes its end state and delta sum as its record;
+    // 2: seeded: the records already hold each segment's incoming state and delta prefix sum
+    //    (written by the fold kernel), so no segment waits or publishes.
+    int mode;
 };
 
 struct PersistPlan {
@@ -123,6 +129,11 @@ struct PersistPlan {
 
 PersistPlan plan_persistent(int64_t B, int64_t L, int64_t D, int num_sms);
 int64_t persistent_ws_bytes(const PersistPlan& pl);
+// Few (batch, 128-channel) chains: K independent segments per chain for the state-only /
+// fold / seeded passes (ok = false when the shape has too few tiles for that).
+PersistPlan plan_persistent_split(int64_t B, int64_t L, int64_t D, int num_sms);
+cudaError_t launch_fwd_persistent_split(PFwdArgs& a, const PersistPlan& pl, int dtype, void* ws,
+                                        cudaStream_t s);
 bool make_tmap_3d(CUtensorMap* map, const void* base, int dtype, int64_t W, int64_t L, int64_t B,
                   int bw, int bl);
 cudaError_t launch_fwd_persistent(PFwdArgs& a, const PersistPlan& pl, int dtype, void* ws,

@@ -130,7 +130,7 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
         return;
     }
     const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
-    const int total = p.nchains * p.K;
+    const int total = p.nchains * (p.mode == 1 ? p.K - 1 : p.K);   // state-only: no last segment
     auto unit_tiles = [&](int k) { return min(p.seg_tiles, p.ntiles - k * p.seg_tiles); };
 
     if (tid == 0) {
@@ -176,14 +176,14 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
             s.unit[st] = pu;
             s.tile[st] = ptile;
             unsigned bytes = tile_bytes;
-            const bool need_hand = ptile == 0 && k > 0;
+            const bool need_hand = ptile == 0 && k > 0 && p.mode != 1;
             const bool need_hprev = ptile == 0 && k == 0 && p.h_prev != nullptr;
             const int nch = min(PF_CPB, p.D - blk * PF_CPB);
             const unsigned rows_bytes = (unsigned)(nch * NSTATE * sizeof(T));
             if (ptile == 0) bytes += rows_bytes + (unsigned)(nch * sizeof(T));
             if (need_hprev) bytes += rows_bytes;
             if (need_hand) {
-                flag_wait(&p.flags[c * p.K + k - 1], PF_NCW, p.err);
+                if (p.mode == 0) flag_wait(&p.flags[c * p.K + k - 1], PF_NCW, p.err);
                 bytes += PF_HAND * 4;
             }
             mbar_expect_tx(&s.full[st], bytes);
@@ -302,11 +302,11 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
             }
             a_nonpos = __all_sync(FULL, nonpos);
             Dd = dv ? to_f(s.Dt[st][ch]) : 0.f;
-            if (k == 0) {
+            if (k == 0 || p.mode == 1) {   // state-only segments after the first start from zero
                 sumd = 0.f;
 #pragma unroll
                 for (int j = 0; j < 4; ++j) h2[j] = make_float2(0.f, 0.f);
-                if (p.h_prev != nullptr && dv) {
+                if (k == 0 && p.h_prev != nullptr && dv) {
 #pragma unroll
                     for (int j = 0; j < 4; ++j)
                         h2[j] = make_float2(to_f(s.Ht[st][ch][n0 + 2 * j]), to_f(s.Ht[st][ch][n0 + 2 * j + 1]));
@@ -383,16 +383,20 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
 
         if (last) {
             if (k < p.K - 1) {
-                float* hs = p.hand + (int64_t)(c * p.K + k) * PF_HAND + ch * (NSTATE + 1);
+                if (p.mode != 2) {   // seeded segments find their records already written
+                    float* hs = p.hand + (int64_t)(c * p.K + k) * PF_HAND + ch * (NSTATE + 1);
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    hs[n0 + 2 * j] = h2[j].x;
-                    hs[n0 + 2 * j + 1] = h2[j].y;
+                    for (int j = 0; j < 4; ++j) {
+                        hs[n0 + 2 * j] = h2[j].x;
+                        hs[n0 + 2 * j + 1] = h2[j].y;
+                    }
+                    if (half == 0) hs[NSTATE] = sumd;
+                    if (p.mode == 0) {
+                        __threadfence();
+                        __syncwarp();
+                        if (lane == 0) atomicAdd(&p.flags[c * p.K + k], 1);
+                    }
                 }
-                if (half == 0) hs[NSTATE] = sumd;
-                __threadfence();
-                __syncwarp();
-                if (lane == 0) atomicAdd(&p.flags[c * p.K + k], 1);
             } else if (dv) {
                 if (p.h_last != nullptr) {
                     T* hl = static_cast<T*>(p.h_last) + ((int64_t)b * p.D + d) * NSTATE + n0;
@@ -412,6 +416,36 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
                 }
             }
         }
+    }
+}
+
+// Fold of the state-only pass's records (few chains, K independent segments per chain).
+// For chain c and (channel, state), record k holds segment k's end state from its own start
+// (segment 0 from h_prev, the others from zero) and its delta sum; afterwards it holds the
+// true state after segment k and the delta sum from the sequence start:
+//   h_k = 2^(A*log2(e) * sumd_k) h_{k-1} + R_k,   S_k = S_{k-1} + sumd_k
+// A segment's decay is the product of its per-step factors, exp(A * sum delta); the clamp is
+// the per-step one applied to the sum, the identity for A <= 0 and delta >= 0.
+template <typename T>
+__global__ void ss_fwd_fold_kernel(float* __restrict__ hand, const T* __restrict__ A, int nblk,
+                                   int nchains, int K, int D) {
+    const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;   // (c, ch, n), n fastest
+    if (tid >= (int64_t)nchains * PF_CPB * NSTATE) return;   // whole warps: the count is a multiple of 2048
+    const int n = (int)(tid % NSTATE);
+    const int ch = (int)((tid / NSTATE) % PF_CPB);
+    const int c = (int)(tid / (NSTATE * PF_CPB));
+    const int64_t d = (int64_t)(c % nblk) * PF_CPB + ch;
+    const float a2 = d < D ? to_f(A[d * NSTATE + n]) * LOG2E : 0.f;
+    float* r = hand + (int64_t)c * K * PF_HAND + ch * (NSTATE + 1);
+    float h = r[n], S = r[NSTATE];
+    for (int k = 1; k < K - 1; ++k) {
+        float* rk = r + (int64_t)k * PF_HAND;
+        const float sk = rk[NSTATE];
+        h = fmaf(ex2(fminf(a2 * sk, ARG2_HI)), h, rk[n]);
+        S += sk;
+        rk[n] = h;
+        __syncwarp();   // every state of the channel has read rk[NSTATE]
+        if (n == 0) rk[NSTATE] = S;
     }
 }
 
@@ -476,6 +510,39 @@ PersistPlan plan_persistent(int64_t B, int64_t L, int64_t D, int num_sms) {
     return pl;
 }
 
+PersistPlan plan_persistent_split(int64_t B, int64_t L, int64_t D, int num_sms) {
+    PersistPlan pl{};
+    pl.nblk = (int)((D + PF_CPB - 1) / PF_CPB);
+    pl.nchains = (int)(B * pl.nblk);
+    pl.ntiles = (int)((L + PF_LT - 1) / PF_LT);
+    pl.ok = false;
+    if (pl.nchains <= 0 || pl.nchains >= num_sms) return pl;
+    // at least one segment per SM; among the segment counts up to ~4x that, the one whose
+    // units fill whole waves best (fewest segments on a tie)
+    const int kmin = std::max(2, (num_sms + pl.nchains - 1) / pl.nchains);
+    int best_k = 0;
+    double best = -1.0;
+    for (int K = kmin; K <= 4 * kmin + 1; ++K) {
+        const int seg = (pl.ntiles + K - 1) / K;
+        if (seg < MWC_FWD_MIN_SEG_TILES) break;
+        if ((pl.ntiles + seg - 1) / seg != K) continue;
+        const int64_t U = (int64_t)pl.nchains * K;
+        const int64_t G = std::min<int64_t>(num_sms, U);
+        const int64_t waves = (U + G - 1) / G;
+        const double eff = (double)U / (double)(G * waves);
+        if (eff > best + 0.01) {
+            best = eff;
+            best_k = K;
+        }
+    }
+    if (best_k < 2) return pl;
+    pl.K = best_k;
+    pl.seg_tiles = (pl.ntiles + best_k - 1) / best_k;
+    pl.grid = (int)std::min<int64_t>(num_sms, (int64_t)pl.nchains * pl.K);
+    pl.ok = true;
+    return pl;
+}
+
 int64_t persistent_ws_bytes(const PersistPlan& pl) {
     const int64_t units = (int64_t)pl.nchains * pl.K;
     const int64_t hdr = ((16 + units * 4) + 255) / 256 * 256;
@@ -516,6 +583,54 @@ cudaError_t launch_fwd_persistent(PFwdArgs& a, const PersistPlan& pl, int dtype,
     a.ntiles = pl.ntiles;
     cudaError_t e = cudaMemsetAsync(ws, 0, (size_t)persistent_ws_header(pl), s);
     if (e != cudaSuccess) return e;
+    if (dtype == 2) return launch_pf<__nv_bfloat16>(a, pl.grid, s);
+    return dtype == 1 ? launch_pf<__half>(a, pl.grid, s) : launch_pf<float>(a, pl.grid, s);
+}
+
+// Few chains: pass 1 scans segments 0..K-2 for their end states only (delta sums always
+// on, no outputs), the fold turns the records into each segment's incoming state, and pass 2
+// runs the full scan with every segment seeded from its record. Each pass has its own unit
+// counter in the header, which is cleared once.
+cudaError_t launch_fwd_persistent_split(PFwdArgs& a, const PersistPlan& pl, int dtype, void* ws,
+                                        cudaStream_t s) {
+    char* w = static_cast<char*>(ws);
+    a.err = reinterpret_cast<int*>(w + 4);
+    a.flags = reinterpret_cast<int*>(w + 16);
+    a.hand = reinterpret_cast<float*>(w + persistent_ws_header(pl));
+    a.nblk = pl.nblk;
+    a.nchains = pl.nchains;
+    a.K = pl.K;
+    a.seg_tiles = pl.seg_tiles;
+    a.ntiles = pl.ntiles;
+    cudaError_t e = cudaMemsetAsync(ws, 0, (size_t)persistent_ws_header(pl), s);
+    if (e != cudaSuccess) return e;
+    PFwdArgs p1 = a;
+    p1.mode = 1;
+    p1.counter = reinterpret_cast<int*>(w);
+    p1.has_out = 0;
+    p1.ckpt = nullptr;
+    p1.h_last = nullptr;
+    p1.decay = nullptr;
+    const int grid1 = (int)std::min<int64_t>(pl.grid, (int64_t)pl.nchains * (pl.K - 1));
+    e = dtype == 2 ? launch_pf_t<__nv_bfloat16, true>(p1, grid1, s)
+      : dtype == 1 ? launch_pf_t<__half, true>(p1, grid1, s)
+                   : launch_pf_t<float, true>(p1, grid1, s);
+    if (e != cudaSuccess) return e;
+    const int64_t nthr = (int64_t)pl.nchains * PF_CPB * NSTATE;
+    const unsigned fb = (unsigned)((nthr + 255) / 256);
+    if (dtype == 2)
+        ss_fwd_fold_kernel<__nv_bfloat16><<<fb, 256, 0, s>>>(a.hand, static_cast<const __nv_bfloat16*>(a.A),
+                                                             pl.nblk, pl.nchains, pl.K, a.D);
+    else if (dtype == 1)
+        ss_fwd_fold_kernel<__half><<<fb, 256, 0, s>>>(a.hand, static_cast<const __half*>(a.A), pl.nblk,
+                                                      pl.nchains, pl.K, a.D);
+    else
+        ss_fwd_fold_kernel<float><<<fb, 256, 0, s>>>(a.hand, static_cast<const float*>(a.A), pl.nblk,
+                                                     pl.nchains, pl.K, a.D);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    a.mode = 2;
+    a.counter = reinterpret_cast<int*>(w + 8);
     if (dtype == 2) return launch_pf<__nv_bfloat16>(a, pl.grid, s);
     return dtype == 1 ? launch_pf<__half>(a, pl.grid, s) : launch_pf<float>(a, pl.grid, s);
 }

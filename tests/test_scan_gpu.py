@@ -370,6 +370,53 @@ def test_persistent_forward_many_chains(mwc, dtype, D, L):
             assert_fp16(grads[k2], ref[k2], k2, atol=2e-2 * scale, rtol=1e-2)
 
 
+@pytest.mark.parametrize("dtype,B,L,D,dist", [(torch.float32, 1, 4096, 2048, "c4"),
+                                               (torch.float16, 2, 3000, 640, "c1"),
+                                               (torch.bfloat16, 1, 2048, 1024, "c1")])
+def test_persistent_forward_few_chains(mwc, dtype, B, L, D, dist):
+    """B*D/128 < #SMs: the persistent kernel scans independent L-segments for their end
+    states, a fold kernel chains them (segment decay exp(A * sum delta)), and a seeded pass
+    writes y, the checkpoints, h_last and the decay. Checked against the oracle, including the
+    gradients the backward computes from those checkpoints."""
+    from mamba_windows_cuda import _lib, _ops
+    dt = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}[dtype]
+    assert _lib.load().mwc_ss_fwd_workspace_bytes(B, L, D, dt) > 0
+    x = make_inputs(B, L, D, dtype, seed=41 + L, with_state=True, dist=dist, device="cuda")
+    args = [x[k] for k in ("u", "delta", "A", "Bm", "Cm", "Dv")]
+    out, h_last, ckpt, decay = _ops.ss_forward(*args, x["h_prev"], want_h_last=True,
+                                               want_ckpt=True, want_decay=True)
+    ref_out, ref_h = oracle_fwd(x, x["h_prev"])
+    f32 = dtype == torch.float32
+    tol16 = 2e-2 if dtype == torch.bfloat16 else 1e-2
+    check = (lambda a, r, w: assert_fp32(a, r, what=w)) if f32 else \
+        (lambda a, r, w: assert_fp16(a, r, w, rtol=tol16))
+    check(out, ref_out, "out")
+    check(h_last, ref_h, "h_last")
+    for k in ((L - 1) // 16 // 3, (L - 1) // 16 - 1):
+        _, h_k = O.ss_fwd(*[np64(x[n][:, :16 * (k + 1)] if n in ("u", "delta", "Bm", "Cm") else x[n])
+                            for n in ("u", "delta", "A", "Bm", "Cm", "Dv")], np64(x["h_prev"]))
+        assert_fp32(ckpt[:, k], h_k, tol=1e-4 if f32 else tol16, what=f"ckpt {k}")
+    ref_decay = torch.exp(x["delta"].double().sum(1).unsqueeze(-1) * x["A"].double().unsqueeze(0))
+    assert_fp32(decay, ref_decay.cpu().numpy(), tol=1e-4 if f32 else tol16, what="decay")
+    _, _, grads = run_stateful(mwc, x, x["h_prev"], x["gh"])
+    ref = oracle_bwd(x, x["h_prev"], x["gh"])
+    for k2 in GRADS + ("dh_prev",):
+        if f32:
+            assert_fp32(grads[k2], ref[k2], what=k2)
+        else:
+            scale = max(1.0, float(np.abs(ref[k2]).max()))
+            assert_fp16(grads[k2], ref[k2], k2, atol=2e-2 * scale, rtol=tol16)
+
+
+def test_persistent_forward_few_chains_deterministic(mwc):
+    from mamba_windows_cuda import _ops
+    x = make_inputs(1, 4096, 1024, torch.float16, seed=8, with_state=True, device="cuda")
+    args = [x[k] for k in ("u", "delta", "A", "Bm", "Cm", "Dv")]
+    o1, h1, c1, _ = _ops.ss_forward(*args, x["h_prev"], want_h_last=True, want_ckpt=True)
+    o2, h2, c2, _ = _ops.ss_forward(*args, x["h_prev"], want_h_last=True, want_ckpt=True)
+    assert torch.equal(o1, o2) and torch.equal(h1, h2) and torch.equal(c1, c2)
+
+
 def test_persistent_backward_is_deterministic(mwc):
     x = make_inputs(4, 300, 5120, torch.float16, seed=9, with_state=True, device="cuda")
     _, _, g1 = run_stateful(mwc, x, x["h_prev"], x["gh"])
