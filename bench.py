@@ -19,6 +19,7 @@ all host threads) on a bounded sample of the same workload (rank 0 only).
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -643,7 +644,8 @@ def bench_conv(args, cfg, dev, world, rank, peaks):
     """Causal conv1d (width 4, SiLU) forward + backward: HBM-bound (x read, y written;
     x, dy read, dx written: 10 bytes per fp16 element, plus the weight / bias partials).
     Roofline: the backward op (TMA-staged kernel + fixed-order weight reduction, the larger
-    share of the step), timed per step with events on the launching stream."""
+    share of the step), timed with events on the launching stream over back-to-back C-ABI
+    calls."""
     from mamba_windows_cuda.causal_conv1d import causal_conv1d_fn
     B, L, D = cfg["B"], cfg["L"], cfg["D"]
     gen = torch.Generator(device=dev).manual_seed(6000 + rank)
@@ -681,12 +683,44 @@ def bench_conv(args, cfg, dev, world, rank, peaks):
     ms = max_over_ranks(start.elapsed_time(stop), world, dev)
     fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
     bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    # The autograd step leaves the GPU idle while Python runs between the two ops, so the
+    # kernels' own durations come from back-to-back C-ABI calls on preallocated buffers
+    # (the backward op: the TMA kernel + the weight reduction; inputs > L2 between calls).
+    from mamba_windows_cuda import _lib
+    from mamba_windows_cuda._ops import _p, dtype_code
+    lib = _lib.load()
+    sh = ctypes.c_void_p(stream.cuda_stream)
+    xd, wd, bd = x.detach(), w.detach(), b.detach()
+    yk = torch.empty_like(xd)
+    dxk, dwk, dbk = torch.empty_like(xd), torch.empty_like(wd), torch.empty_like(bd)
+    wsb = int(lib.mwc_conv1d_bwd_workspace_bytes(B, L, D, 4))
+    wsk = torch.empty(max(wsb, 1), dtype=torch.uint8, device=dev)
+    dc = dtype_code(xd)
+
+    def kfwd():
+        return lib.mwc_conv1d_fwd(_p(xd), _p(wd), _p(bd), None, 1, _p(yk), B, L, D, 4, dc, sh)
+
+    def kbwd():
+        return lib.mwc_conv1d_bwd(_p(xd), _p(wd), _p(bd), None, 1, _p(dy), _p(dxk), _p(dwk), _p(dbk), None,
+                                  _p(wsk), wsb, B, L, D, 4, dc, sh)
+
+    kms = {}
+    for name, fn in (("fwd", kfwd), ("bwd", kbwd)):
+        for _ in range(3):
+            assert fn() == 0, name
+        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        k0.record(stream)
+        for _ in range(args.steps):
+            fn()
+        k1.record(stream)
+        torch.cuda.synchronize(dev)
+        kms[name] = k0.elapsed_time(k1) / args.steps
     es = x.element_size()
     E = B * L * D
     nbytes = 10 * E * es // 2
     bwd_bytes = 3 * E * es + 4 * D * es * 2   # x, dy read, dx written; weights in, dweight out
     t = ms / args.steps / 1e3
-    achieved = bwd_bytes / (bwd_ms / 1e3) / 1e9
+    achieved = bwd_bytes / (kms["bwd"] / 1e3) / 1e9
     roofline = {"kernel": "conv1d_bwd_tma_kernel + conv1d_reduce_kernel (backward op)",
                 "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": achieved / peaks["hbm_gbs"],
@@ -694,8 +728,8 @@ def bench_conv(args, cfg, dev, world, rank, peaks):
                 "traffic_source": CAPTURED_TRAFFIC["conv"]["source"] if args.config == "conv" else None,
                 "peak_source": peaks["source"],
                 "model": "x, dy read + dx written (3 x 2 B per fp16 element)",
-                "per_op_ms": {"fwd": fwd_ms, "bwd": bwd_ms},
-                "fwd_frac": 2 * E * es / (fwd_ms / 1e3) / 1e9 / peaks["hbm_gbs"]}
+                "kernel_ms": kms, "per_op_ms_in_step": {"fwd": fwd_ms, "bwd": bwd_ms},
+                "fwd_frac": 2 * E * es / (kms["fwd"] / 1e3) / 1e9 / peaks["hbm_gbs"]}
     xh, dyh = x.detach().cpu().pin_memory(), dy.cpu().pin_memory()
     dxh = torch.empty(x.shape, dtype=dt).pin_memory()
 

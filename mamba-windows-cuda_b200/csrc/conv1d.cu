@@ -27,6 +27,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
@@ -68,6 +69,53 @@ __device__ __forceinline__ void cv_store(T* p, const float (&v)[VEC]) {
 // result is 0 once exp(-x) passes 2^126, i.e. x < -87, where the true value is below 1e-38)
 __device__ __forceinline__ float cv_sigmoid(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
 
+// s[q] = init[q] + sum_kk a[kk][q] * b[kk][q], accumulated in kk order. Channel pairs go
+// through one packed fma.rn.f32x2; each of its lanes rounds like fmaf, so the result is
+// bitwise the scalar chain (the element path, with one channel per thread, runs that chain).
+template <int W, int V>
+__device__ __forceinline__ void cv_taps(const float (&a)[W][V], const float (&b)[W][V], const float (&init)[V],
+                                        float (&s)[V]) {
+    if constexpr (V % 2 == 0) {
+#pragma unroll
+        for (int q = 0; q < V; q += 2) {
+            float2 acc = make_float2(init[q], init[q + 1]);
+#pragma unroll
+            for (int kk = 0; kk < W; ++kk)
+                acc = __ffma2_rn(make_float2(a[kk][q], a[kk][q + 1]), make_float2(b[kk][q], b[kk][q + 1]), acc);
+            s[q] = acc.x;
+            s[q + 1] = acc.y;
+        }
+    } else {
+#pragma unroll
+        for (int q = 0; q < V; ++q) {
+            float acc = init[q];
+#pragma unroll
+            for (int kk = 0; kk < W; ++kk) acc = fmaf(a[kk][q], b[kk][q], acc);
+            s[q] = acc;
+        }
+    }
+}
+
+// acc[kk][q] += x[q] * y[kk][q] for every tap (packed by channel pairs, like cv_taps)
+template <int W, int V>
+__device__ __forceinline__ void cv_accum(float (&acc)[W][V], const float (&x)[V], const float (&y)[W][V]) {
+#pragma unroll
+    for (int kk = 0; kk < W; ++kk) {
+        if constexpr (V % 2 == 0) {
+#pragma unroll
+            for (int q = 0; q < V; q += 2) {
+                const float2 r = __ffma2_rn(make_float2(x[q], x[q + 1]), make_float2(y[kk][q], y[kk][q + 1]),
+                                            make_float2(acc[kk][q], acc[kk][q + 1]));
+                acc[kk][q] = r.x;
+                acc[kk][q + 1] = r.y;
+            }
+        } else {
+#pragma unroll
+            for (int q = 0; q < V; ++q) acc[kk][q] = fmaf(x[q], y[kk][q], acc[kk][q]);
+        }
+    }
+}
+
 // x at time t (t may be negative: from x_prev, or zero)
 template <typename T, int VEC, int W>
 __device__ __forceinline__ void cv_x_at(const T* x, const T* x_prev, int64_t b, int64_t t, int64_t L, int64_t D,
@@ -103,12 +151,10 @@ __global__ void __launch_bounds__(CV_THREADS) conv1d_fwd_kernel(const T* __restr
     for (int64_t t = t0; t < t1; ++t) {
         cv_load<T, VEC>(x + (b * L + t) * D + d0, win[W - 1]);
         float o[VEC];
+        cv_taps<W, VEC>(wk, win, bv, o);
+        if (act) {
 #pragma unroll
-        for (int c = 0; c < VEC; ++c) {
-            float s = bv[c];
-#pragma unroll
-            for (int k = 0; k < W; ++k) s = fmaf(wk[k][c], win[k][c], s);
-            o[c] = act ? s * cv_sigmoid(s) : s;
+            for (int c = 0; c < VEC; ++c) o[c] = o[c] * cv_sigmoid(o[c]);
         }
         cv_store<T, VEC>(y + (b * L + t) * D + d0, o);
 #pragma unroll
@@ -123,15 +169,14 @@ template <int VEC, int W>
 __device__ __forceinline__ void cv_dpre(const float (&wk)[W][VEC], const float (&bv)[VEC], const float (&xw)[W][VEC],
                                         const float (&g)[VEC], int act, float (&dp)[VEC]) {
 #pragma unroll
-    for (int c = 0; c < VEC; ++c) {
-        float s = bv[c];
+    for (int c = 0; c < VEC; ++c) dp[c] = g[c];
+    if (act) {
+        float pre[VEC];
+        cv_taps<W, VEC>(wk, xw, bv, pre);
 #pragma unroll
-        for (int k = 0; k < W; ++k) s = fmaf(wk[k][c], xw[k][c], s);
-        if (act) {
-            const float sg = cv_sigmoid(s);
-            dp[c] = g[c] * sg * (1.f + s * (1.f - sg));
-        } else {
-            dp[c] = g[c];
+        for (int c = 0; c < VEC; ++c) {
+            const float sg = cv_sigmoid(pre[c]);
+            dp[c] = g[c] * sg * (1.f + pre[c] * (1.f - sg));
         }
     }
 }
@@ -175,11 +220,8 @@ __global__ void __launch_bounds__(CV_THREADS) conv1d_bwd_kernel(
             cv_dpre<VEC, W>(wk, bv, xw, g, act, dp);
             if (s < t1) {
 #pragma unroll
-                for (int c = 0; c < VEC; ++c) {
-                    ab[c] += dp[c];
-#pragma unroll
-                    for (int k = 0; k < W; ++k) aw[k][c] = fmaf(dp[c], xw[k][c], aw[k][c]);
-                }
+                for (int c = 0; c < VEC; ++c) ab[c] += dp[c];
+                cv_accum<W, VEC>(aw, dp, xw);
             }
         } else {
 #pragma unroll
@@ -423,12 +465,10 @@ __global__ void __launch_bounds__(CT_THREADS + 32, CT_FWD_CTAS_PER_SM) conv1d_fw
         for (int i = 0; i < R; ++i) {
             ct_ld<T, P>(sx + (r0 + CT_HALO + i) * CC, win[W - 1]);
             float o[P];
+            cv_taps<W, P>(wk, win, bv, o);
+            if (act) {
 #pragma unroll
-            for (int q = 0; q < P; ++q) {
-                float s = bv[q];
-#pragma unroll
-                for (int kk = 0; kk < W; ++kk) s = fmaf(wk[kk][q], win[kk][q], s);
-                o[q] = act ? s * cv_sigmoid(s) : s;
+                for (int q = 0; q < P; ++q) o[q] = o[q] * cv_sigmoid(o[q]);
             }
             const int t = t0 + r0 + i;
             if (valid && t < L) ct_st<T, P>(y + ((int64_t)b * L + t) * D + c, o);
@@ -446,14 +486,13 @@ __global__ void __launch_bounds__(CT_THREADS + 32, CT_FWD_CTAS_PER_SM) conv1d_fw
 template <typename T, int W, int P>
 __device__ __forceinline__ void cv_dx_emit(const float (&wk)[W][P], const float (&dq)[W][P], bool do_store,
                                            T* dst) {
-    float o[P];
+    float o[P], rq[W][P];
+    const float zero[P] = {};
 #pragma unroll
-    for (int q = 0; q < P; ++q) {
-        float a = 0.f;
+    for (int kk = 0; kk < W; ++kk)
 #pragma unroll
-        for (int kk = 0; kk < W; ++kk) a = fmaf(wk[kk][q], dq[W - 1 - kk][q], a);
-        o[q] = a;
-    }
+        for (int q = 0; q < P; ++q) rq[kk][q] = dq[W - 1 - kk][q];
+    cv_taps<W, P>(wk, rq, zero, o);
     if (do_store) ct_st<T, P>(dst, o);
 }
 
@@ -550,11 +589,8 @@ __global__ void __launch_bounds__(CT_THREADS + 32, 2) conv1d_bwd_tma_kernel(
             ct_ld<T, P>(sg + (r0 + i) * CC, g);
             cv_dpre<P, W>(wk, bv, win, g, act, dp);
 #pragma unroll
-            for (int q = 0; q < P; ++q) {
-                ab[q] += dp[q];
-#pragma unroll
-                for (int kk = 0; kk < W; ++kk) aw[kk][q] = fmaf(dp[q], win[kk][q], aw[kk][q]);
-            }
+            for (int q = 0; q < P; ++q) ab[q] += dp[q];
+            cv_accum<W, P>(aw, dp, win);
             if (i < W - 1)   // the first W-1 dpre complete dx of the row group below
                 ct_st<float, P>(xb + (rg * CT_HALO + i) * CC + col * P, dp);
 #pragma unroll
@@ -717,7 +753,7 @@ static cudaError_t ct_fwd_launch(const CUtensorMap& tm, const void* w, const voi
     const int nseg = std::max(1, std::min(nitems, sms * CT_FWD_CTAS_PER_SM / ncb));
     const size_t smem = (size_t)CT_FWD_ST * (CT_TT + CT_HALO) * CT_ROWB + 2 * CT_FWD_ST * sizeof(uint64_t);
     auto kern = conv1d_fwd_tma_kernel<T, W>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = ensure_smem_attr<conv1d_fwd_tma_kernel<T, W>>((int)smem);
     if (e != cudaSuccess) return e;
     kern<<<(unsigned)ncb * nseg, CT_THREADS + 32, smem, s>>>(
         tm, static_cast<const T*>(w), static_cast<const T*>(bias), static_cast<const T*>(x_prev), act,
@@ -742,7 +778,7 @@ static cudaError_t ct_bwd_launch(const CUtensorMap& tmx, const CUtensorMap& tmg,
     const size_t smem = (size_t)CT_BWD_ST * ((CT_TT + 2 * CT_HALO) + (CT_TT + CT_HALO)) * CT_ROWB +
                         2 * (size_t)Sh::G * CT_HALO * Sh::CC * sizeof(float) + 2 * CT_BWD_ST * sizeof(uint64_t);
     auto kern = conv1d_bwd_tma_kernel<T, W>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = ensure_smem_attr<conv1d_bwd_tma_kernel<T, W>>((int)smem);
     if (e != cudaSuccess) return e;
     kern<<<(unsigned)ncb * nseg, CT_THREADS + 32, smem, s>>>(
         tmx, tmg, static_cast<const T*>(w), static_cast<const T*>(bias), static_cast<const T*>(x_prev), act,
@@ -784,8 +820,17 @@ static bool ct_sizes_ok(int64_t B, int64_t L, int64_t D, int64_t es) {
 }
 
 static const int* ct_err_word() {
+    static std::atomic<const int*> cache[64];   // per device ordinal
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+    if (dev >= 0 && dev < 64) {
+        const int* w = cache[dev].load(std::memory_order_relaxed);
+        if (w != nullptr) return w;
+    }
     void* p = nullptr;
-    return cudaGetSymbolAddress(&p, g_cv_err) == cudaSuccess ? static_cast<const int*>(p) : nullptr;
+    if (cudaGetSymbolAddress(&p, g_cv_err) != cudaSuccess) return nullptr;
+    if (dev >= 0 && dev < 64) cache[dev].store(static_cast<const int*>(p), std::memory_order_relaxed);
+    return static_cast<const int*>(p);
 }
 
 static int cv_check(int dtype, int64_t B, int64_t L, int64_t D, int64_t W, int act) {

@@ -1,6 +1,8 @@
 // Host-side launch interface between the C ABI (capi.cu) and the kernel files.
 #pragma once
 
+#include <atomic>
+
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -173,6 +175,21 @@ cudaError_t launch_bwd_persistent(PBwdArgs& a, const PersistPlan& pl, int dtype,
 // Error reporting shared by the C entry points (capi.cu).
 int report_error(int code, const char* msg);
 int report_ok();
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device): the attribute
+// persists in the context, and setting it on every launch costs a driver call.
+template <auto Kern>
+inline cudaError_t ensure_smem_attr(int bytes) {
+    static std::atomic<int> done[64];   // bytes already allowed, per device ordinal
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const bool cached = dev >= 0 && dev < 64;
+    if (cached && done[dev].load(std::memory_order_relaxed) >= bytes) return cudaSuccess;
+    e = cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess && cached) done[dev].store(bytes, std::memory_order_relaxed);
+    return e;
+}
+
 // Error word that mwc_check_last_launch reads for the last launch on this thread (nullptr: none).
 void note_err_word(const int* word);
 int current_device_sms();

@@ -828,8 +828,7 @@ static cudaError_t launch_pb(const PBwdArgs& a, int grid, void* dA, void* dB, vo
     // more than half of the SM's shared memory: one CTA per SM, so the CTA's 512-column TMEM
     // allocation never waits for another CTA of this kernel
     const size_t smem = std::max(sizeof(PBwdSmem<T>), (size_t)(120 * 1024));
-    cudaError_t e = cudaFuncSetAttribute(ss_bwd_persistent_kernel<T>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = ensure_smem_attr<ss_bwd_persistent_kernel<T>>((int)smem);
     if (e != cudaSuccess) return e;
     ss_bwd_persistent_kernel<T><<<grid, PB_NT, smem, s>>>(a);
     e = cudaGetLastError();

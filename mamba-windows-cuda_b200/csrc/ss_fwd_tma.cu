@@ -557,8 +557,7 @@ int64_t persistent_ws_header(const PersistPlan& pl) {
 template <typename T, bool DECAY>
 static cudaError_t launch_pf_t(const PFwdArgs& a, int grid, cudaStream_t s) {
     const size_t smem = sizeof(PFwdSmem<T>);
-    cudaError_t e = cudaFuncSetAttribute(ss_fwd_persistent_kernel<T, DECAY>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = ensure_smem_attr<ss_fwd_persistent_kernel<T, DECAY>>((int)smem);
     if (e != cudaSuccess) return e;
     ss_fwd_persistent_kernel<T, DECAY><<<grid, PF_NT, smem, s>>>(a);
     return cudaGetLastError();
