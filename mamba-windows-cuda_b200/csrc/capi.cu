@@ -217,7 +217,8 @@ int mwc_ss_fwd(const void* u, const void* delta, const void* A, const void* Bm, 
 int64_t mwc_ss_bwd_workspace_bytes(int64_t B, int64_t L, int64_t D, int dtype) {
     if (B <= 0 || L <= 0 || D <= 0) return 0;
     int64_t need = bwd_ws(B, L, D, dtype).total;
-    const PersistPlan pb = plan_persistent_bwd(B, L, D, device_sms());
+    PersistPlan pb = plan_persistent_bwd(B, L, D, device_sms());
+    if (!pb.ok) pb = plan_persistent_bwd_split(B, L, D, device_sms());
     if (pb.ok) need = std::max<int64_t>(need, bwd_persistent_ws(pb, B, L).total);
     return need;
 }
@@ -241,7 +242,10 @@ int mwc_ss_bwd(const void* u, const void* delta, const void* A, const void* Bm, 
     if (B == 0 || D == 0) return ok();
     {
         const size_t es0 = elem_size(dtype);
-        const PersistPlan pb = plan_persistent_bwd(B, L, D, device_sms());
+        // many chains: chained segments; few chains: adjoint-only pass, fold, seeded pass
+        const PersistPlan pchain = plan_persistent_bwd(B, L, D, device_sms());
+        const bool split = !pchain.ok;
+        const PersistPlan pb = split ? plan_persistent_bwd_split(B, L, D, device_sms()) : pchain;
         const bool tma_ok = pb.ok && ((D * (int64_t)es0) % 16 == 0) && aligned16(u) &&
                             aligned16(delta) && aligned16(dout) && aligned16(Bm) &&
                             aligned16(Cm) && aligned16(A) && aligned16(du) && aligned16(ddelta) &&
@@ -267,8 +271,10 @@ int mwc_ss_bwd(const void* u, const void* delta, const void* A, const void* Bm, 
                 pa.A = A; pa.Dv = Dv; pa.h_prev = h_prev; pa.dh_last = dh_last; pa.ckpt = ckpt;
                 pa.du = du; pa.ddelta = ddelta; pa.dh_prev = dh_prev;
                 pa.B = (int)B; pa.L = (int)L; pa.D = (int)D; pa.nck = (int)nck;
-                cudaError_t e = launch_bwd_persistent(pa, pb, dtype, workspace, dA, dB, dC, dD,
-                                                      static_cast<cudaStream_t>(stream));
+                cudaStream_t st = static_cast<cudaStream_t>(stream);
+                cudaError_t e = split ? launch_bwd_persistent_split(pa, pb, dtype, workspace, delta, dout, Cm,
+                                                                    dA, dB, dC, dD, st)
+                                      : launch_bwd_persistent(pa, pb, dtype, workspace, dA, dB, dC, dD, st);
                 if (e != cudaSuccess) return cuda_fail(e, "selective-scan persistent backward launch");
                 g_last_err_word = pa.err;
                 return ok();

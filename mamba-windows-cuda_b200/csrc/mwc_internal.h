@@ -161,14 +161,26 @@ struct PBwdArgs {
     int* err;
     int B, L, D;
     int nblk, nchains, K, seg_tiles, ntiles, nck;
+    // 0: chained segments (segment k waits for the adjoint state segment k+1 publishes);
+    // 2: seeded: the records already hold the adjoint state at each segment's end (written
+    //    by the adjoint-only pass and its fold), so no segment waits or publishes.
+    int mode;
 };
 
 struct BwdPersistWs {
-    int64_t off_hand, off_a, off_d, off_bc, total;
+    int64_t off_hand, off_a, off_d, off_bc, off_sum, total;
 };
 
 PersistPlan plan_persistent_bwd(int64_t B, int64_t L, int64_t D, int num_sms);
 BwdPersistWs bwd_persistent_ws(const PersistPlan& pl, int64_t B, int64_t L);
+// Few chains: K independent segments per chain for the adjoint-only / fold / seeded passes.
+PersistPlan plan_persistent_bwd_split(int64_t B, int64_t L, int64_t D, int num_sms);
+cudaError_t launch_bwd_persistent_split(PBwdArgs& a, const PersistPlan& pl, int dtype, void* ws,
+                                        const void* delta, const void* dout, const void* Cm,
+                                        void* dA, void* dB, void* dC, void* dD, cudaStream_t s);
+// Segment count for the few-chain split passes: the K (2..ntiles/min_seg) minimising
+// waves x segment length, plus a small per-segment term; 0 when no K fits.
+int pick_split_segments(int nchains, int ntiles, int num_sms, int min_seg_tiles);
 cudaError_t launch_bwd_persistent(PBwdArgs& a, const PersistPlan& pl, int dtype, void* ws,
                                   void* dA, void* dB, void* dC, void* dD, cudaStream_t s);
 

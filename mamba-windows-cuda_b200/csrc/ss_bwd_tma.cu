@@ -271,8 +271,8 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                 if (kp > 0) {
                     // the tile is already on its way; the adjoint state of the successor
                     // segment follows on its own barrier, which the compute warps wait for
-                    // only after their recompute pass
-                    flag_wait(&p.flags[c * p.K + kp - 1], PB_NCW, p.err);
+                    // only after their recompute pass (seeded: the record is already there)
+                    if (p.mode == 0) flag_wait(&p.flags[c * p.K + kp - 1], PB_NCW, p.err);
                     fence_proxy_async_global();
                     mbar_expect_tx(&s.qfull[st], (unsigned)(PB_CPB * NSTATE * 4));
                     bulk_load(&s.qin[st][0][0], p.hand + (int64_t)(c * p.K + kp - 1) * PB_CPB * NSTATE,
@@ -706,14 +706,16 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                     make_float4(dA[cc][0].x, dA[cc][0].y, dA[cc][1].x, dA[cc][1].y);
             if (sg == 0) *reinterpret_cast<float2*>(p.ws_d + ub) = make_float2(dD[0], dD[1]);
             if (k > 0) {
-                float* hs = p.hand + ((int64_t)(c * p.K + kp) * PB_CPB + c2) * NSTATE + 4 * sg;
+                if (p.mode == 0) {   // seeded segments find the records already written
+                    float* hs = p.hand + ((int64_t)(c * p.K + kp) * PB_CPB + c2) * NSTATE + 4 * sg;
 #pragma unroll
-                for (int cc = 0; cc < 2; ++cc)
-                    *reinterpret_cast<float4*>(hs + cc * NSTATE) =
-                        make_float4(q[cc][0].x, q[cc][0].y, q[cc][1].x, q[cc][1].y);
-                __threadfence();
-                __syncwarp();
-                if (lane == 0) atomicAdd(&p.flags[c * p.K + kp], 1);
+                    for (int cc = 0; cc < 2; ++cc)
+                        *reinterpret_cast<float4*>(hs + cc * NSTATE) =
+                            make_float4(q[cc][0].x, q[cc][0].y, q[cc][1].x, q[cc][1].y);
+                    __threadfence();
+                    __syncwarp();
+                    if (lane == 0) atomicAdd(&p.flags[c * p.K + kp], 1);
+                }
             } else if (p.dh_prev != nullptr) {
 #pragma unroll
                 for (int cc = 0; cc < 2; ++cc)
@@ -777,6 +779,128 @@ __global__ void ss_bwd_persistent_final_kernel(const __grid_constant__ PBwdArgs 
     }
 }
 
+// ------------------------------------------------------------ few-chain split passes
+// Pass 1: for segment k >= 1 of chain c (unit kp = K-1-k, walked last step first), the
+// adjoint state at the segment's start when q = 0 at its end (dh_last for the last segment):
+//   q <- a_t (dout_t C_t + q),  a_t = 2^(delta_t A log2 e)   (the reference's adjoint without
+// the gradient terms, mamba_windows_cuda/mamba_cuda.py:703-742), and the segment's delta sum.
+// Thread = (channel, half): 8 of the channel's 16 states; the CTA stages 32-step tiles of
+// delta / dout (32 x 128, 16-byte vectors: rows of D * elem are 16-byte multiples on this
+// path) and C (32 x 16, float32) in shared memory.
+constexpr int AJ_LT = 32;
+
+template <typename T>
+__global__ void __launch_bounds__(256) ss_bwd_adjoint_kernel(
+    const T* __restrict__ delta, const T* __restrict__ dout, const T* __restrict__ Cm, const T* __restrict__ A,
+    const T* __restrict__ dh_last, float* __restrict__ hand, float* __restrict__ segsum, int L, int D, int nblk,
+    int nchains, int K, int seg_tiles) {
+    constexpr int VE = 16 / (int)sizeof(T);   // elements per 16-byte vector
+    constexpr int VPR = PB_CPB / VE;          // vectors per 128-channel row
+    __shared__ __align__(16) T sd[AJ_LT][PB_CPB];
+    __shared__ __align__(16) T sgy[AJ_LT][PB_CPB];
+    __shared__ __align__(16) float sC[AJ_LT][NSTATE];
+    const int unit = blockIdx.x;   // kp * nchains + c
+    const int c = unit % nchains, kp = unit / nchains, k = K - 1 - kp;
+    const int b = c / nblk, blk = c % nblk;
+    const int tstart = k * seg_tiles * PB_LT;
+    const int tend = min(tstart + seg_tiles * PB_LT, L);
+    const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
+    const int ch = w * 16 + (lane >> 1), n0 = (lane & 1) * 8;
+    const int64_t d = (int64_t)blk * PB_CPB + ch;
+    const bool dv = d < D;
+    float A2[8], q[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        A2[j] = dv ? to_f(A[d * NSTATE + n0 + j]) * LOG2E : 0.f;
+        q[j] = (kp == 0 && dh_last != nullptr && dv) ? to_f(dh_last[((int64_t)b * D + d) * NSTATE + n0 + j]) : 0.f;
+    }
+    float sumd = 0.f;
+    const int ntl = (tend - tstart + AJ_LT - 1) / AJ_LT;
+    for (int ti = ntl - 1; ti >= 0; --ti) {
+        const int t0 = tstart + ti * AJ_LT;
+        const int nr = min(AJ_LT, tend - t0);
+        __syncthreads();   // the previous tile is no longer read
+        for (int idx = tid; idx < AJ_LT * VPR; idx += 256) {
+            const int r = idx / VPR, v = idx % VPR;
+            const int64_t dd = (int64_t)blk * PB_CPB + v * VE;
+            uint4 a4 = make_uint4(0u, 0u, 0u, 0u), g4 = a4;
+            if (r < nr && dd < D) {
+                const int64_t off = ((int64_t)b * L + t0 + r) * D + dd;
+                a4 = *reinterpret_cast<const uint4*>(delta + off);
+                g4 = *reinterpret_cast<const uint4*>(dout + off);
+            }
+            *reinterpret_cast<uint4*>(&sd[r][v * VE]) = a4;
+            *reinterpret_cast<uint4*>(&sgy[r][v * VE]) = g4;
+        }
+        for (int idx = tid; idx < AJ_LT * NSTATE; idx += 256) {
+            const int r = idx / NSTATE, n = idx % NSTATE;
+            sC[r][n] = r < nr ? to_f(Cm[((int64_t)b * L + t0 + r) * NSTATE + n]) : 0.f;
+        }
+        __syncthreads();
+#pragma unroll 4
+        for (int r = nr - 1; r >= 0; --r) {
+            const float dt = to_f(sd[r][ch]), gy = to_f(sgy[r][ch]);
+            sumd += dt;
+            const float4* Cq = reinterpret_cast<const float4*>(&sC[r][n0]);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const float4 c4 = Cq[h];
+                const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int jj = 4 * h + j;
+                    const float a = ex2(fminf(dt * A2[jj], ARG2_HI));
+                    q[jj] = a * fmaf(gy, cv[j], q[jj]);
+                }
+            }
+        }
+    }
+    float* rec = hand + ((int64_t)(c * K + kp) * PB_CPB + ch) * NSTATE + n0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) rec[j] = q[j];
+    if ((lane & 1) == 0) segsum[(int64_t)(c * K + kp) * PB_CPB + ch] = sumd;
+}
+
+// Fold of the adjoint records in reverse time: record kp (segment K-1-kp) holds q at the
+// segment's start from q = 0 at its end (the last segment from dh_last, so record 0 is
+// exact); afterwards record kp holds the true q at that point:
+//   Q_kp = 2^(A log2(e) * sumd_kp) Q_{kp-1} + R_kp   (a segment's decay is exp(A * sum delta))
+template <typename T>
+__global__ void ss_bwd_fold_kernel(float* __restrict__ hand, const float* __restrict__ segsum,
+                                   const T* __restrict__ A, int nblk, int nchains, int K, int D) {
+    const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;   // (c, ch, n), n fastest
+    if (tid >= (int64_t)nchains * PB_CPB * NSTATE) return;
+    const int n = (int)(tid % NSTATE);
+    const int ch = (int)((tid / NSTATE) % PB_CPB);
+    const int c = (int)(tid / (NSTATE * PB_CPB));
+    const int64_t d = (int64_t)(c % nblk) * PB_CPB + ch;
+    const float a2 = d < D ? to_f(A[d * NSTATE + n]) * LOG2E : 0.f;
+    float* r = hand + ((int64_t)c * K * PB_CPB + ch) * NSTATE + n;
+    const float* sm = segsum + (int64_t)c * K * PB_CPB + ch;
+    float Q = r[0];
+    for (int kp = 1; kp < K - 1; ++kp) {
+        Q = fmaf(ex2(fminf(a2 * sm[(int64_t)kp * PB_CPB], ARG2_HI)), Q, r[(int64_t)kp * PB_CPB * NSTATE]);
+        r[(int64_t)kp * PB_CPB * NSTATE] = Q;
+    }
+}
+
+PersistPlan plan_persistent_bwd_split(int64_t B, int64_t L, int64_t D, int num_sms) {
+    PersistPlan pl{};
+    pl.nblk = (int)((D + PB_CPB - 1) / PB_CPB);
+    pl.nchains = (int)(B * pl.nblk);
+    pl.ntiles = (int)((L + PB_LT - 1) / PB_LT);
+    pl.ok = false;
+    // below ~512 steps one generic pass is as fast as three short launches
+    if (pl.nchains <= 0 || pl.nchains >= num_sms || (int64_t)pl.ntiles * PB_LT < 512) return pl;
+    const int K = pick_split_segments(pl.nchains, pl.ntiles, num_sms, 2);
+    if (K < 2) return pl;
+    pl.K = K;
+    pl.seg_tiles = (pl.ntiles + K - 1) / K;
+    pl.grid = (int)std::min<int64_t>(num_sms, (int64_t)pl.nchains * K);
+    pl.ok = true;
+    return pl;
+}
+
 PersistPlan plan_persistent_bwd(int64_t B, int64_t L, int64_t D, int num_sms) {
     PersistPlan pl{};
     pl.nblk = (int)((D + PB_CPB - 1) / PB_CPB);
@@ -814,7 +938,8 @@ BwdPersistWs bwd_persistent_ws(const PersistPlan& pl, int64_t B, int64_t L) {
     w.off_d = w.off_a + up(units * PB_CPB * NSTATE * 4);
     w.off_bc = w.off_d + up(units * PB_CPB * 4);
     const int64_t Lp = (L + CK - 1) / CK * CK;
-    w.total = w.off_bc + up((int64_t)pl.nblk * B * Lp * 2 * NSTATE * 4);
+    w.off_sum = w.off_bc + up((int64_t)pl.nblk * B * Lp * 2 * NSTATE * 4);
+    w.total = w.off_sum + up(units * PB_CPB * 4);   // per-segment delta sums (split passes)
     return w;
 }
 
@@ -860,6 +985,52 @@ cudaError_t launch_bwd_persistent(PBwdArgs& a, const PersistPlan& pl, int dtype,
     if (dtype == 2) return launch_pb<__nv_bfloat16>(a, pl.grid, dA, dB, dC, dD, s);
     return dtype == 1 ? launch_pb<__half>(a, pl.grid, dA, dB, dC, dD, s)
                       : launch_pb<float>(a, pl.grid, dA, dB, dC, dD, s);
+}
+
+// Few chains: the adjoint-only pass over segments K-1..1, the fold, then the ordinary
+// backward with every segment seeded from its record (mode 2).
+template <typename T>
+static cudaError_t bwd_split_passes(PBwdArgs& a, const PersistPlan& pl, float* segsum, const void* delta,
+                                    const void* dout, const void* Cm, void* dA, void* dB, void* dC, void* dD,
+                                    cudaStream_t s) {
+    const T* At = static_cast<const T*>(a.A);
+    ss_bwd_adjoint_kernel<T><<<(unsigned)(pl.nchains * (pl.K - 1)), 256, 0, s>>>(
+        static_cast<const T*>(delta), static_cast<const T*>(dout), static_cast<const T*>(Cm), At,
+        static_cast<const T*>(a.dh_last), a.hand, segsum, a.L, a.D, pl.nblk, pl.nchains, pl.K, pl.seg_tiles);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    const int64_t nthr = (int64_t)pl.nchains * PB_CPB * NSTATE;
+    ss_bwd_fold_kernel<T><<<(unsigned)((nthr + 255) / 256), 256, 0, s>>>(a.hand, segsum, At, pl.nblk, pl.nchains,
+                                                                       pl.K, a.D);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    return launch_pb<T>(a, pl.grid, dA, dB, dC, dD, s);
+}
+
+cudaError_t launch_bwd_persistent_split(PBwdArgs& a, const PersistPlan& pl, int dtype, void* ws,
+                                        const void* delta, const void* dout, const void* Cm,
+                                        void* dA, void* dB, void* dC, void* dD, cudaStream_t s) {
+    const BwdPersistWs w = bwd_persistent_ws(pl, a.B, a.L);
+    char* base = static_cast<char*>(ws);
+    a.counter = reinterpret_cast<int*>(base);
+    a.err = reinterpret_cast<int*>(base + 4);
+    a.flags = reinterpret_cast<int*>(base + 16);
+    a.hand = reinterpret_cast<float*>(base + w.off_hand);
+    a.ws_a = reinterpret_cast<float*>(base + w.off_a);
+    a.ws_d = reinterpret_cast<float*>(base + w.off_d);
+    a.ws_bc = reinterpret_cast<float*>(base + w.off_bc);
+    float* segsum = reinterpret_cast<float*>(base + w.off_sum);
+    a.nblk = pl.nblk;
+    a.nchains = pl.nchains;
+    a.K = pl.K;
+    a.seg_tiles = pl.seg_tiles;
+    a.ntiles = pl.ntiles;
+    a.mode = 2;
+    cudaError_t e = cudaMemsetAsync(ws, 0, (size_t)w.off_hand, s);
+    if (e != cudaSuccess) return e;
+    if (dtype == 2) return bwd_split_passes<__nv_bfloat16>(a, pl, segsum, delta, dout, Cm, dA, dB, dC, dD, s);
+    if (dtype == 1) return bwd_split_passes<__half>(a, pl, segsum, delta, dout, Cm, dA, dB, dC, dD, s);
+    return bwd_split_passes<float>(a, pl, segsum, delta, dout, Cm, dA, dB, dC, dD, s);
 }
 
 }  // namespace mwc

@@ -510,34 +510,37 @@ PersistPlan plan_persistent(int64_t B, int64_t L, int64_t D, int num_sms) {
     return pl;
 }
 
+int pick_split_segments(int nchains, int ntiles, int num_sms, int min_seg_tiles) {
+    // time ~ waves x segment length (units of one pass run in parallel); the small term per
+    // segment stands for the records, the fold and each unit's start-up
+    int best_k = 0;
+    double best = 1e300;
+    for (int K = 2; K <= ntiles / min_seg_tiles; ++K) {
+        const int seg = (ntiles + K - 1) / K;
+        if ((ntiles + seg - 1) / seg != K) continue;
+        const int64_t U = (int64_t)nchains * K;
+        const int64_t waves = (U + num_sms - 1) / num_sms;
+        const double cost = (double)waves * seg + 0.02 * K;
+        if (cost < best - 1e-9) {
+            best = cost;
+            best_k = K;
+        }
+    }
+    return best_k;
+}
+
 PersistPlan plan_persistent_split(int64_t B, int64_t L, int64_t D, int num_sms) {
     PersistPlan pl{};
     pl.nblk = (int)((D + PF_CPB - 1) / PF_CPB);
     pl.nchains = (int)(B * pl.nblk);
     pl.ntiles = (int)((L + PF_LT - 1) / PF_LT);
     pl.ok = false;
-    if (pl.nchains <= 0 || pl.nchains >= num_sms) return pl;
-    // at least one segment per SM; among the segment counts up to ~4x that, the one whose
-    // units fill whole waves best (fewest segments on a tie)
-    const int kmin = std::max(2, (num_sms + pl.nchains - 1) / pl.nchains);
-    int best_k = 0;
-    double best = -1.0;
-    for (int K = kmin; K <= 4 * kmin + 1; ++K) {
-        const int seg = (pl.ntiles + K - 1) / K;
-        if (seg < MWC_FWD_MIN_SEG_TILES) break;
-        if ((pl.ntiles + seg - 1) / seg != K) continue;
-        const int64_t U = (int64_t)pl.nchains * K;
-        const int64_t G = std::min<int64_t>(num_sms, U);
-        const int64_t waves = (U + G - 1) / G;
-        const double eff = (double)U / (double)(G * waves);
-        if (eff > best + 0.01) {
-            best = eff;
-            best_k = K;
-        }
-    }
-    if (best_k < 2) return pl;
-    pl.K = best_k;
-    pl.seg_tiles = (pl.ntiles + best_k - 1) / best_k;
+    // below ~512 steps one generic pass is as fast as three short launches
+    if (pl.nchains <= 0 || pl.nchains >= num_sms || (int64_t)pl.ntiles * PF_LT < 512) return pl;
+    const int K = pick_split_segments(pl.nchains, pl.ntiles, num_sms, MWC_FWD_MIN_SEG_TILES);
+    if (K < 2) return pl;
+    pl.K = K;
+    pl.seg_tiles = (pl.ntiles + K - 1) / K;
     pl.grid = (int)std::min<int64_t>(num_sms, (int64_t)pl.nchains * pl.K);
     pl.ok = true;
     return pl;
