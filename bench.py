@@ -405,33 +405,15 @@ def bench_fwdbwd(args, cfg, dev, world, rank, peaks):
     }
 
     # e2e through the public API from pinned host memory
-    host_in = [t.detach().cpu().pin_memory() for t in ins]
-    host_g = gy.cpu().pin_memory()
+    host_in = [t.detach().cpu().pin_memory() for t in ins] + [gy.cpu().pin_memory()]
     host_out = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in ins]
-    h2d = sum(t.numel() * t.element_size() for t in host_in) + host_g.numel() * host_g.element_size()
-    d2h = sum(t.numel() * t.element_size() for t in host_out)
 
-    def e2e_step():
-        xs = [h.to(dev, non_blocking=True).requires_grad_(True) for h in host_in]
-        g_d = host_g.to(dev, non_blocking=True)
-        out = mod(*xs)
-        out.backward(g_d)
-        for ho, x in zip(host_out, xs):
-            ho.copy_(x.grad, non_blocking=True)
+    def e2e_op(xs):
+        leaves_d = [x.detach().requires_grad_(True) for x in xs[:-1]]
+        mod(*leaves_d).backward(xs[-1])
+        return [x.grad for x in leaves_d]
 
-    e2e_steps = max(3, min(args.steps, 10))
-    for _ in range(2):
-        e2e_step()
-    barrier_sync(world, dev)
-    s2, t2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s2.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
-    t2.record(stream)
-    torch.cuda.synchronize(dev)
-    e2e_ms = max_over_ranks(s2.elapsed_time(t2), world, dev) / e2e_steps
-    e2e = {"value": nbytes * world / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
-           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms}
+    e2e = _e2e(args, world, dev, host_in, host_out, e2e_op, nbytes)
     return dict(value=value, ms_per_step=ms_max / args.steps, roofline=roofline, e2e=e2e,
                 clocks=clk.summary(), gpu_launches=launches_per_step * args.steps,
                 dtype="f32", io_dtype=str(cfg["dtype"]).replace("torch.", ""))
@@ -551,29 +533,58 @@ def _timed(args, world, dev, fn):
 
 
 def _e2e(args, world, dev, host_in, host_out, fn_dev, nbytes):
-    """Same op through host buffers: H2D of the step's inputs, the op, D2H of its outputs,
-    all inside the timed region."""
-    stream = torch.cuda.current_stream(dev)
+    """Same op through host buffers, as a training or inference loop feeds it: every step
+    copies its inputs host -> device from pinned memory, runs the op through the public API
+    and copies its results device -> host, all inside the timed region. The copies run on
+    their own streams, so step i+1's inputs load (into the other of two device buffer sets)
+    while step i computes and step i-1's results drain; PCIe carries both directions at
+    once. fn_dev gets the step's device inputs and returns the device outputs."""
+    comp = torch.cuda.current_stream(dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    bufs = [[torch.empty(h.shape, dtype=h.dtype, device=dev) for h in host_in] for _ in range(2)]
+    ready = [torch.cuda.Event() for _ in range(2)]
+    free = [torch.cuda.Event() for _ in range(2)]
 
-    def step():
-        outs = fn_dev([h.to(dev, non_blocking=True) for h in host_in])
-        for ho, o in zip(host_out, outs):
-            ho.copy_(o, non_blocking=True)
+    def load(j):
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(free[j])   # the op that last read buffer set j is done
+            for bd, h in zip(bufs[j], host_in):
+                bd.copy_(h, non_blocking=True)
+            ready[j].record(s_in)
+
+    def run(n):
+        for j in range(2):
+            free[j].record(comp)
+        s_in.wait_stream(comp)
+        load(0)
+        for i in range(n):
+            j = i % 2
+            if i + 1 < n:
+                load((i + 1) % 2)
+            comp.wait_event(ready[j])
+            outs = fn_dev(bufs[j])
+            free[j].record(comp)
+            s_out.wait_stream(comp)
+            with torch.cuda.stream(s_out):
+                for ho, o in zip(host_out, outs):
+                    o.record_stream(s_out)   # keep the result alive until its copy is done
+                    ho.copy_(o, non_blocking=True)
+        comp.wait_stream(s_out)
 
     steps = max(3, min(args.steps, 10))
-    for _ in range(2):
-        step()
+    run(2)
+    torch.cuda.synchronize(dev)
     barrier_sync(world, dev)
     s2, t2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s2.record(stream)
-    for _ in range(steps):
-        step()
-    t2.record(stream)
+    s2.record(comp)
+    run(steps)
+    t2.record(comp)
     torch.cuda.synchronize(dev)
     ms = max_over_ranks(s2.elapsed_time(t2), world, dev) / steps
     return {"value": nbytes * world / (ms / 1e3) / 1e9, "unit": "GB/s",
             "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in host_in),
-            "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in host_out), "ms_per_step": ms}
+            "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in host_out), "ms_per_step": ms,
+            "overlap": "step i+1 host->device and step i-1 device->host copies overlap step i"}
 
 
 def bench_fwd(args, cfg, dev, world, rank, peaks):
@@ -734,7 +745,7 @@ def bench_conv(args, cfg, dev, world, rank, peaks):
     dxh = torch.empty(x.shape, dtype=dt).pin_memory()
 
     def op(xs):
-        xi = xs[0].requires_grad_(True)
+        xi = xs[0].detach().requires_grad_(True)
         causal_conv1d_fn(xi, w, b, "silu").backward(xs[1])
         return (xi.grad,)
 
