@@ -314,6 +314,24 @@ def reference_arm(args, cfg):
 
 # ----------------------------------------------------------------------------- GPU arms
 
+def scan_launches(B, L, D, es, dev):
+    """(forward, backward) kernel launches of one scan call, by the library's own rule:
+    B*D/128 chains >= SMs run the chained persistent kernels (1 forward; backward + its
+    finalize); fewer chains with 16-byte rows and L >= 512 run the split passes (state-only
+    pass, fold, seeded pass; adjoint-only pass, fold, seeded backward, finalize); other
+    shapes the generic kernels (forward + fixup when L is segmented; backward + finalize).
+    The bench's inputs are 16-byte aligned."""
+    from mamba_windows_cuda import _lib
+    nch = B * ((D + 127) // 128)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    if nch >= sms:
+        return 1, 2
+    if (D * es) % 16 == 0 and L >= 512:
+        return 3, 4
+    seg = int(_lib.load().mwc_ss_fwd_workspace_bytes(B, L, D, 0 if es == 4 else 1)) > 0
+    return (2 if seg else 1), 2
+
+
 def bench_fwdbwd(args, cfg, dev, world, rank, peaks):
     import mamba_windows_cuda as mwc
     B, L, D = cfg["B"], cfg["L"], cfg["D"]
@@ -370,10 +388,8 @@ def bench_fwdbwd(args, cfg, dev, world, rank, peaks):
     # our kernels per step: the forward scan (+ its carry fixup on the segmented path), the
     # backward scan + its finalize; the block form adds the delta transform and the gate in
     # both directions and the ddelta / dbias pair
-    nch = B * ((D + 127) // 128)
-    sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    seg_fwd = nch < sms and int(mwc._lib.load().mwc_ss_fwd_workspace_bytes(B, L, D, 0 if es == 4 else 1)) > 0
-    launches_per_step = (2 if seg_fwd else 1) + 2 + (6 if block else 0)
+    fk, bk = scan_launches(B, L, D, es, dev)
+    launches_per_step = fk + bk + (6 if block else 0)
 
     # roofline of the dominant kernel (the backward: reverse scan + its fixed-order reduction)
     mufu_peak = 148 * 16 * peaks["sm_max_mhz"] * 1e6  # ex2 / s at the max SM clock
@@ -438,8 +454,6 @@ def bench_stream(args, cfg, dev, world, rank, peaks):
     h0 = torch.zeros(B, D, NSTATE, dtype=cfg["dtype"], device=dev) if rank == 0 else None
     mod = mwc.SelectiveScanCuda()
     stream = torch.cuda.current_stream(dev)
-    lib = mwc._lib.load()
-    dcode = 1 if es == 2 else 0
 
     if world == 1:
         def step():
@@ -449,15 +463,13 @@ def bench_stream(args, cfg, dev, world, rank, peaks):
                     sl = slice(c * Lc, (c + 1) * Lc)
                     _, h = mod.forward_with_state(u[:, sl], delta[:, sl], A, Bm[:, sl], Cm[:, sl], Dv, h)
             return h
-        per_call = 1 if int(lib.mwc_ss_fwd_workspace_bytes(B, Lc, D, dcode)) == 0 else 2
-        launches = nch * per_call
+        launches = nch * scan_launches(B, Lc, D, es, dev)[0]
     else:
         def step():
             with torch.no_grad():
                 _, h = S.sequence_sharded_forward(u, delta, A, Bm, Cm, Dv, h0)
             return h
-        per_call = 1 if int(lib.mwc_ss_fwd_workspace_bytes(B, Lr, D, dcode)) == 0 else 2
-        launches = per_call + (1 if rank > 0 else 0)
+        launches = scan_launches(B, Lr, D, es, dev)[0] + (1 if rank > 0 else 0)
 
     for _ in range(args.warmup):
         step()
