@@ -581,19 +581,19 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                     float2 s1, s2;
 #pragma unroll
                     for (int pr = 0; pr < 2; ++pr) {
-                        const float2 a = av[cc][pr];
                         const float2 g = __ffma2_rn(gy2, Cp[pr], q[cc][pr]);
-                        const float2 pp = __fmul2_rn(g, __fmul2_rn(a, hp[cc][pr]));
+                        // q_{t-1} = a g, and p = g a h_{t-1} = q_{t-1} h_{t-1} reuses it
+                        const float2 qn = __fmul2_rn(av[cc][pr], g);
+                        const float2 pp = __fmul2_rn(qn, hp[cc][pr]);
                         s1 = pr == 0 ? __fmul2_rn(A2[cc][pr], pp) : __ffma2_rn(A2[cc][pr], pp, s1);
                         s2 = pr == 0 ? __fmul2_rn(g, Bp[pr]) : __ffma2_rn(g, Bp[pr], s2);
                         dA[cc][pr] = __ffma2_rn(dt2, pp, dA[cc][pr]);
                         vB[pr] = cc == 0 ? __fmul2_rn(g, du2) : __ffma2_rn(g, du2, vB[pr]);
                         vC[pr] = cc == 0 ? __fmul2_rn(gy2, ht[cc][pr]) : __ffma2_rn(gy2, ht[cc][pr], vC[pr]);
-                        q[cc][pr] = __fmul2_rn(a, g);
+                        q[cc][pr] = qn;
                     }
                     sv[r][cc] = s1.x + s1.y;
                     sv[r][2 + cc] = s2.x + s2.y;
-                    dD[cc] = fmaf(gy[r][cc], uu[r][cc], dD[cc]);
                 }
                 vv[r][0] = vB[0].x; vv[r][1] = vB[0].y; vv[r][2] = vB[1].x; vv[r][3] = vB[1].y;
                 vv[r][4] = vC[0].x; vv[r][5] = vC[0].y; vv[r][6] = vC[1].x; vv[r][7] = vC[1].y;
@@ -633,6 +633,9 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                 load2<T>(gq, &s.g[st][i][c2]);
                 const float du0 = fmaf(gq[0], Dd[0], dq[0] * sv[0][2]);
                 const float du1 = fmaf(gq[1], Dd[1], dq[1] * sv[0][3]);
+                // dD = sum_t dout u: lane sg takes the steps i0 + sg (summed over sg at the unit end)
+                dD[0] = fmaf(gq[0], uq[0], dD[0]);
+                dD[1] = fmaf(gq[1], uq[1], dD[1]);
                 const float dd0 = fmaf(uq[0], sv[0][2], sv[0][0] * LN2);
                 const float dd1 = fmaf(uq[1], sv[0][3], sv[0][1] * LN2);
                 if constexpr (Cfg::STAGE_OUT) {
@@ -704,6 +707,11 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
             for (int cc = 0; cc < 2; ++cc)
                 *reinterpret_cast<float4*>(p.ws_a + (ub + cc) * NSTATE + 4 * sg) =
                     make_float4(dA[cc][0].x, dA[cc][0].y, dA[cc][1].x, dA[cc][1].y);
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) {   // the 4 state-group lanes hold every 4th step
+                dD[cc] += __shfl_xor_sync(FULL, dD[cc], 1);
+                dD[cc] += __shfl_xor_sync(FULL, dD[cc], 2);
+            }
             if (sg == 0) *reinterpret_cast<float2*>(p.ws_d + ub) = make_float2(dD[0], dD[1]);
             if (k > 0) {
                 if (p.mode == 0) {   // seeded segments find the records already written
