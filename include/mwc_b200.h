@@ -115,6 +115,25 @@ MWC_API int mwc_ss_fixup(const void* delta, const void* A, const void* Cm, const
                  int64_t B, int64_t L, int64_t D, int dtype, void* stream);
 
 /*
+ * mwc_ss_fwd_grouped / mwc_ss_bwd_grouped -- mwc_ss_fwd / mwc_ss_bwd with B_ssm and C_ssm (and
+ * dB, dC) of shape (B, L, G, 16): channel d reads group d / (D / G). No counterpart in the
+ * reference, whose B / C are (B, L, 16) (G = 1, where these equal mwc_ss_fwd / mwc_ss_bwd);
+ * the official Mamba scan takes grouped B / C. G must divide D, D / G must be a multiple of
+ * 128, and the shape must take the persistent path (16-byte-aligned buffers, rows of
+ * D x element size a multiple of 16 bytes, and B*D/128 >= SM count or L >= 512); otherwise
+ * MWC_ERR_UNSUPPORTED. Workspace sizes as for mwc_ss_fwd / mwc_ss_bwd.
+ */
+MWC_API int mwc_ss_fwd_grouped(const void* u, const void* delta, const void* A, const void* Bm,
+               const void* Cm, const void* Dv, const void* h_prev, void* out, void* h_last,
+               float* ckpt, float* decay, void* workspace, int64_t workspace_bytes,
+               int64_t B, int64_t L, int64_t D, int64_t G, int dtype, void* stream);
+MWC_API int mwc_ss_bwd_grouped(const void* u, const void* delta, const void* A, const void* Bm,
+               const void* Cm, const void* Dv, const void* h_prev, const void* dout,
+               const void* dh_last, const float* ckpt, void* du, void* ddelta, void* dA, void* dB,
+               void* dC, void* dD, void* dh_prev, void* workspace, int64_t workspace_bytes,
+               int64_t B, int64_t L, int64_t D, int64_t G, int dtype, void* stream);
+
+/*
  * First-order linear recurrence along axis 2 of (B, D, L, N) = (R, L, N) with R = B*D:
  * h_0 = x_0 (a_0 ignored), h_t = a_t h_{t-1} + x_t. Replaces PScan.forward /
  * parallel_scan_fn (mamba_windows_cuda/pscan.py:16-150), with the semantics of

@@ -133,14 +133,34 @@ int64_t mwc_ss_fwd_workspace_bytes(int64_t B, int64_t L, int64_t D, int dtype) {
     return need;
 }
 
-int mwc_ss_fwd(const void* u, const void* delta, const void* A, const void* Bm, const void* Cm,
-               const void* Dv, const void* h_prev, void* out, void* h_last, float* ckpt,
-               float* decay, void* workspace, int64_t workspace_bytes, int64_t B, int64_t L,
-               int64_t D, int dtype, void* stream) {
+// B / C groups: G = 1 is the reference's (B, L, 16) layout; G > 1 gives (B, L, G, 16) with
+// channel d in group d / (D / G), supported on the persistent paths when D / G is a
+// multiple of the 128-channel block.
+static int check_groups(int64_t D, int64_t G) {
+    if (G < 1 || D % G != 0) return fail(MWC_ERR_INVALID, "groups must divide D (D=%lld, G=%lld)",
+                                         (long long)D, (long long)G);
+    if (G > 1 && (D / G) % 128 != 0)
+        return fail(MWC_ERR_UNSUPPORTED, "grouped B / C need D / G to be a multiple of 128 (D=%lld, G=%lld)",
+                    (long long)D, (long long)G);
+    return MWC_OK;
+}
+
+static int fail_groups_path() {
+    return fail(MWC_ERR_UNSUPPORTED,
+                "grouped B / C run on the persistent path only: 16-byte-aligned buffers, rows of "
+                "D x element size a multiple of 16 bytes, and at least as many (batch, 128-channel) "
+                "chains as SMs or L >= 512");
+}
+
+static int ss_fwd_impl(const void* u, const void* delta, const void* A, const void* Bm, const void* Cm,
+                       const void* Dv, const void* h_prev, void* out, void* h_last, float* ckpt,
+                       float* decay, void* workspace, int64_t workspace_bytes, int64_t B, int64_t L,
+                       int64_t D, int64_t G, int dtype, void* stream) {
     g_last_err_word = nullptr;
     int rc;
     if ((rc = check_dtype(dtype)) != MWC_OK) return rc;
     if ((rc = check_sizes(B, L, D)) != MWC_OK) return rc;
+    if ((rc = check_groups(D, G)) != MWC_OK) return rc;
     if (!u || !delta || !A || !Bm || !Cm || !Dv)
         return fail(MWC_ERR_INVALID, "u, delta, A, B_ssm, C_ssm and D_ssm are required");
     if (!out && !h_last && !ckpt && !decay)
@@ -167,10 +187,11 @@ int mwc_ss_fwd(const void* u, const void* delta, const void* A, const void* Bm, 
         PFwdArgs pa{};
         bool maps = make_tmap_3d(&pa.tm_u, u, dtype, D, L, B, 128, 32) &&
                     make_tmap_3d(&pa.tm_d, delta, dtype, D, L, B, 128, 32) &&
-                    make_tmap_3d(&pa.tm_B, Bm, dtype, NSTATE, L, B, NSTATE, 32) &&
-                    make_tmap_3d(&pa.tm_C, Cm, dtype, NSTATE, L, B, NSTATE, 32) &&
+                    make_tmap_3d(&pa.tm_B, Bm, dtype, G * NSTATE, L, B, NSTATE, 32) &&
+                    make_tmap_3d(&pa.tm_C, Cm, dtype, G * NSTATE, L, B, NSTATE, 32) &&
                     make_tmap_3d(&pa.tm_y, out ? out : u, dtype, D, L, B, 128, 32);
         if (maps) {
+            pa.G = (int)G; pa.cpg = (int)(D / G);
             pa.A = A; pa.Dv = Dv; pa.h_prev = h_prev; pa.h_last = h_last;
             pa.ckpt = ckpt; pa.decay = decay;
             pa.B = (int)B; pa.L = (int)L; pa.D = (int)D;
@@ -184,6 +205,7 @@ int mwc_ss_fwd(const void* u, const void* delta, const void* A, const void* Bm, 
             return ok();
         }
     }
+    if (G > 1) return fail_groups_path();
     const FwdPlan plan = plan_fwd(B, L, D, dtype, sms);
     const int64_t need = align_up(fwd_carry_floats(plan, B, D) * 4, 256);
     if (need > 0 && (!workspace || workspace_bytes < need))
@@ -214,6 +236,22 @@ int mwc_ss_fwd(const void* u, const void* delta, const void* A, const void* Bm, 
     return ok();
 }
 
+int mwc_ss_fwd(const void* u, const void* delta, const void* A, const void* Bm, const void* Cm,
+               const void* Dv, const void* h_prev, void* out, void* h_last, float* ckpt,
+               float* decay, void* workspace, int64_t workspace_bytes, int64_t B, int64_t L,
+               int64_t D, int dtype, void* stream) {
+    return ss_fwd_impl(u, delta, A, Bm, Cm, Dv, h_prev, out, h_last, ckpt, decay, workspace,
+                       workspace_bytes, B, L, D, 1, dtype, stream);
+}
+
+int mwc_ss_fwd_grouped(const void* u, const void* delta, const void* A, const void* Bm,
+                       const void* Cm, const void* Dv, const void* h_prev, void* out, void* h_last,
+                       float* ckpt, float* decay, void* workspace, int64_t workspace_bytes,
+                       int64_t B, int64_t L, int64_t D, int64_t G, int dtype, void* stream) {
+    return ss_fwd_impl(u, delta, A, Bm, Cm, Dv, h_prev, out, h_last, ckpt, decay, workspace,
+                       workspace_bytes, B, L, D, G, dtype, stream);
+}
+
 int64_t mwc_ss_bwd_workspace_bytes(int64_t B, int64_t L, int64_t D, int dtype) {
     if (B <= 0 || L <= 0 || D <= 0) return 0;
     int64_t need = bwd_ws(B, L, D, dtype).total;
@@ -223,15 +261,16 @@ int64_t mwc_ss_bwd_workspace_bytes(int64_t B, int64_t L, int64_t D, int dtype) {
     return need;
 }
 
-int mwc_ss_bwd(const void* u, const void* delta, const void* A, const void* Bm, const void* Cm,
-               const void* Dv, const void* h_prev, const void* dout, const void* dh_last,
-               const float* ckpt, void* du, void* ddelta, void* dA, void* dB, void* dC, void* dD,
-               void* dh_prev, void* workspace, int64_t workspace_bytes, int64_t B, int64_t L,
-               int64_t D, int dtype, void* stream) {
+static int ss_bwd_impl(const void* u, const void* delta, const void* A, const void* Bm, const void* Cm,
+                       const void* Dv, const void* h_prev, const void* dout, const void* dh_last,
+                       const float* ckpt, void* du, void* ddelta, void* dA, void* dB, void* dC, void* dD,
+                       void* dh_prev, void* workspace, int64_t workspace_bytes, int64_t B, int64_t L,
+                       int64_t D, int64_t G, int dtype, void* stream) {
     g_last_err_word = nullptr;
     int rc;
     if ((rc = check_dtype(dtype)) != MWC_OK) return rc;
     if ((rc = check_sizes(B, L, D)) != MWC_OK) return rc;
+    if ((rc = check_groups(D, G)) != MWC_OK) return rc;
     if (!u || !delta || !A || !Bm || !Cm || !Dv || !dout)
         return fail(MWC_ERR_INVALID, "u, delta, A, B_ssm, C_ssm, D_ssm and dout are required");
     if (!du || !ddelta || !dA || !dB || !dC || !dD)
@@ -263,14 +302,15 @@ int mwc_ss_bwd(const void* u, const void* delta, const void* A, const void* Bm, 
             const bool maps = make_tmap_3d(&pa.tm_u, u, dtype, D, L, B, 128, CK) &&
                               make_tmap_3d(&pa.tm_d, delta, dtype, D, L, B, 128, CK) &&
                               make_tmap_3d(&pa.tm_g, dout, dtype, D, L, B, 128, CK) &&
-                              make_tmap_3d(&pa.tm_B, Bm, dtype, NSTATE, L, B, NSTATE, CK) &&
-                              make_tmap_3d(&pa.tm_C, Cm, dtype, NSTATE, L, B, NSTATE, CK) &&
+                              make_tmap_3d(&pa.tm_B, Bm, dtype, G * NSTATE, L, B, NSTATE, CK) &&
+                              make_tmap_3d(&pa.tm_C, Cm, dtype, G * NSTATE, L, B, NSTATE, CK) &&
                               make_tmap_3d(&pa.tm_du, du, dtype, D, L, B, 128, CK) &&
                               make_tmap_3d(&pa.tm_dd, ddelta, dtype, D, L, B, 128, CK);
             if (maps) {
                 pa.A = A; pa.Dv = Dv; pa.h_prev = h_prev; pa.dh_last = dh_last; pa.ckpt = ckpt;
                 pa.du = du; pa.ddelta = ddelta; pa.dh_prev = dh_prev;
                 pa.B = (int)B; pa.L = (int)L; pa.D = (int)D; pa.nck = (int)nck;
+                pa.G = (int)G; pa.cpg = (int)(D / G);
                 cudaStream_t st = static_cast<cudaStream_t>(stream);
                 cudaError_t e = split ? launch_bwd_persistent_split(pa, pb, dtype, workspace, delta, dout, Cm,
                                                                     dA, dB, dC, dD, st)
@@ -281,6 +321,7 @@ int mwc_ss_bwd(const void* u, const void* delta, const void* A, const void* Bm, 
             }
         }
     }
+    if (G > 1) return fail_groups_path();
     const BwdWs w = bwd_ws(B, L, D, dtype);
     if (!workspace || workspace_bytes < w.total)
         return fail(MWC_ERR_WORKSPACE, "backward workspace of %lld bytes required, got %lld",
@@ -309,6 +350,25 @@ int mwc_ss_bwd(const void* u, const void* delta, const void* A, const void* Bm, 
     e = launch_bwd_final(f, dtype, s);
     if (e != cudaSuccess) return cuda_fail(e, "selective-scan backward reduction launch");
     return ok();
+}
+
+int mwc_ss_bwd(const void* u, const void* delta, const void* A, const void* Bm, const void* Cm,
+               const void* Dv, const void* h_prev, const void* dout, const void* dh_last,
+               const float* ckpt, void* du, void* ddelta, void* dA, void* dB, void* dC, void* dD,
+               void* dh_prev, void* workspace, int64_t workspace_bytes, int64_t B, int64_t L,
+               int64_t D, int dtype, void* stream) {
+    return ss_bwd_impl(u, delta, A, Bm, Cm, Dv, h_prev, dout, dh_last, ckpt, du, ddelta, dA, dB, dC,
+                       dD, dh_prev, workspace, workspace_bytes, B, L, D, 1, dtype, stream);
+}
+
+int mwc_ss_bwd_grouped(const void* u, const void* delta, const void* A, const void* Bm,
+                       const void* Cm, const void* Dv, const void* h_prev, const void* dout,
+                       const void* dh_last, const float* ckpt, void* du, void* ddelta, void* dA,
+                       void* dB, void* dC, void* dD, void* dh_prev, void* workspace,
+                       int64_t workspace_bytes, int64_t B, int64_t L, int64_t D, int64_t G,
+                       int dtype, void* stream) {
+    return ss_bwd_impl(u, delta, A, Bm, Cm, Dv, h_prev, dout, dh_last, ckpt, du, ddelta, dA, dB, dC,
+                       dD, dh_prev, workspace, workspace_bytes, B, L, D, G, dtype, stream);
 }
 
 int mwc_ss_fixup(const void* delta, const void* A, const void* Cm, const float* h_in,

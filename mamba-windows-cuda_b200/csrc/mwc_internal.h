@@ -116,6 +116,7 @@ struct PFwdArgs {
     int B, L, D;
     int nblk, nchains, K, seg_tiles, ntiles, nck;
     int has_out;
+    int G, cpg;      // B / C groups (B_ssm, C_ssm are (B, L, G, 16)) and channels per group
     // 0: chained segments (segment k waits for the record segment k-1 publishes);
     // 1: state only: segments 0..K-2 scan independently (segment 0 from h_prev, the others
     //    from zero) and each writes its end state and delta sum as its record;
@@ -161,6 +162,7 @@ struct PBwdArgs {
     int* err;
     int B, L, D;
     int nblk, nchains, K, seg_tiles, ntiles, nck;
+    int G, cpg;      // B / C groups (B_ssm, C_ssm, dB, dC are (B, L, G, 16)), channels per group
     // 0: chained segments (segment k waits for the adjoint state segment k+1 publishes);
     // 2: seeded: the records already hold the adjoint state at each segment's end (written
     //    by the adjoint-only pass and its fold), so no segment waits or publishes.

@@ -257,8 +257,9 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
             tma_load_3d(&s.u[st][0][0], &p.tm_u, &s.full[st], blk * PB_CPB, t0, b);
             tma_load_3d(&s.d[st][0][0], &p.tm_d, &s.full[st], blk * PB_CPB, t0, b);
             tma_load_3d(&s.g[st][0][0], &p.tm_g, &s.full[st], blk * PB_CPB, t0, b);
-            tma_load_3d(&s.Bt[st][0][0], &p.tm_B, &s.full[st], 0, t0, b);
-            tma_load_3d(&s.Ct[st][0][0], &p.tm_C, &s.full[st], 0, t0, b);
+            const int gx = (blk * PB_CPB / p.cpg) * NSTATE;   // the block's B / C group
+            tma_load_3d(&s.Bt[st][0][0], &p.tm_B, &s.full[st], gx, t0, b);
+            tma_load_3d(&s.Ct[st][0][0], &p.tm_C, &s.full[st], gx, t0, b);
             if (tix > 0)
                 bulk_load(&s.h0[st][0][0],
                           p.ckpt + (((int64_t)b * p.nck + tix - 1) * p.D + (int64_t)blk * PB_CPB) * NSTATE,
@@ -751,8 +752,9 @@ template <typename T>
 __global__ void ss_bwd_persistent_final_kernel(const __grid_constant__ PBwdArgs p, void* dA_,
                                                void* dB_, void* dC_, void* dD_) {
     const int64_t Lp = (int64_t)p.nck * CK;
-    const int64_t n_bc = (int64_t)p.B * p.L * 2 * NSTATE;
+    const int64_t n_bc = (int64_t)p.B * p.L * p.G * 2 * NSTATE;
     const int64_t n_a = (int64_t)p.D * NSTATE;
+    const int bpg = p.G > 1 ? p.cpg / PB_CPB : p.nblk;   // blocks per B / C group
     const int64_t total = n_bc + n_a + p.D;
     T* dA = static_cast<T*>(dA_);
     T* dB = static_cast<T*>(dB_);
@@ -761,14 +763,17 @@ __global__ void ss_bwd_persistent_final_kernel(const __grid_constant__ PBwdArgs 
     for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
          idx += (int64_t)gridDim.x * blockDim.x) {
         if (idx < n_bc) {
+            // (b, t, g, v): the sum over the 128-channel blocks of group g, in block order
             const int64_t v = idx % (2 * NSTATE);
-            const int64_t bt = idx / (2 * NSTATE);
+            const int64_t btg = idx / (2 * NSTATE);
+            const int g = (int)(btg % p.G);
+            const int64_t bt = btg / p.G;
             const int64_t b = bt / p.L, t = bt % p.L;
             float s = 0.f;
-            for (int blk = 0; blk < p.nblk; ++blk)
+            for (int blk = g * bpg; blk < (g + 1) * bpg; ++blk)
                 s += p.ws_bc[(((int64_t)blk * p.B + b) * Lp + t) * (2 * NSTATE) + v];
-            if (v < NSTATE) dB[bt * NSTATE + v] = from_f<T>(s);
-            else dC[bt * NSTATE + v - NSTATE] = from_f<T>(s);
+            if (v < NSTATE) dB[btg * NSTATE + v] = from_f<T>(s);
+            else dC[btg * NSTATE + v - NSTATE] = from_f<T>(s);
         } else {
             const bool isA = idx < n_bc + n_a;
             const int64_t i = isA ? idx - n_bc : idx - n_bc - n_a;
@@ -801,7 +806,7 @@ template <typename T>
 __global__ void __launch_bounds__(256) ss_bwd_adjoint_kernel(
     const T* __restrict__ delta, const T* __restrict__ dout, const T* __restrict__ Cm, const T* __restrict__ A,
     const T* __restrict__ dh_last, float* __restrict__ hand, float* __restrict__ segsum, int L, int D, int nblk,
-    int nchains, int K, int seg_tiles) {
+    int nchains, int K, int seg_tiles, int G, int cpg) {
     constexpr int VE = 16 / (int)sizeof(T);   // elements per 16-byte vector
     constexpr int VPR = PB_CPB / VE;          // vectors per 128-channel row
     __shared__ __align__(16) T sd[AJ_LT][PB_CPB];
@@ -810,6 +815,7 @@ __global__ void __launch_bounds__(256) ss_bwd_adjoint_kernel(
     const int unit = blockIdx.x;   // kp * nchains + c
     const int c = unit % nchains, kp = unit / nchains, k = K - 1 - kp;
     const int b = c / nblk, blk = c % nblk;
+    const int grp = blk * PB_CPB / cpg;   // the block's C group
     const int tstart = k * seg_tiles * PB_LT;
     const int tend = min(tstart + seg_tiles * PB_LT, L);
     const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
@@ -842,7 +848,7 @@ __global__ void __launch_bounds__(256) ss_bwd_adjoint_kernel(
         }
         for (int idx = tid; idx < AJ_LT * NSTATE; idx += 256) {
             const int r = idx / NSTATE, n = idx % NSTATE;
-            sC[r][n] = r < nr ? to_f(Cm[((int64_t)b * L + t0 + r) * NSTATE + n]) : 0.f;
+            sC[r][n] = r < nr ? to_f(Cm[(((int64_t)b * L + t0 + r) * G + grp) * NSTATE + n]) : 0.f;
         }
         __syncthreads();
 #pragma unroll 4
@@ -966,7 +972,7 @@ static cudaError_t launch_pb(const PBwdArgs& a, int grid, void* dA, void* dB, vo
     ss_bwd_persistent_kernel<T><<<grid, PB_NT, smem, s>>>(a);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    const int64_t total = (int64_t)a.B * a.L * 2 * NSTATE + (int64_t)a.D * NSTATE + a.D;
+    const int64_t total = (int64_t)a.B * a.L * a.G * 2 * NSTATE + (int64_t)a.D * NSTATE + a.D;
     int64_t blocks = std::min<int64_t>((total + 255) / 256, 148 * 8);
     ss_bwd_persistent_final_kernel<T><<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, s>>>(a, dA, dB, dC, dD);
     return cudaGetLastError();
@@ -1004,7 +1010,8 @@ static cudaError_t bwd_split_passes(PBwdArgs& a, const PersistPlan& pl, float* s
     const T* At = static_cast<const T*>(a.A);
     ss_bwd_adjoint_kernel<T><<<(unsigned)(pl.nchains * (pl.K - 1)), 256, 0, s>>>(
         static_cast<const T*>(delta), static_cast<const T*>(dout), static_cast<const T*>(Cm), At,
-        static_cast<const T*>(a.dh_last), a.hand, segsum, a.L, a.D, pl.nblk, pl.nchains, pl.K, pl.seg_tiles);
+        static_cast<const T*>(a.dh_last), a.hand, segsum, a.L, a.D, pl.nblk, pl.nchains, pl.K, pl.seg_tiles,
+        a.G, a.cpg);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     const int64_t nthr = (int64_t)pl.nchains * PB_CPB * NSTATE;

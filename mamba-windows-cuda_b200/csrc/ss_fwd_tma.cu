@@ -199,8 +199,10 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
                              rows_bytes, &s.full[st]);
             tma_load_3d(&s.u[st][0][0], &p.tm_u, &s.full[st], blk * PF_CPB, t0, b);
             tma_load_3d(&s.d[st][0][0], &p.tm_d, &s.full[st], blk * PF_CPB, t0, b);
-            tma_load_3d(&s.Bt[st][0][0], &p.tm_B, &s.full[st], 0, t0, b);
-            if (p.has_out) tma_load_3d(&s.Ct[st][0][0], &p.tm_C, &s.full[st], 0, t0, b);
+            // the block's B / C group (a 128-channel block lies inside one group)
+            const int gx = (blk * PF_CPB / p.cpg) * NSTATE;
+            tma_load_3d(&s.Bt[st][0][0], &p.tm_B, &s.full[st], gx, t0, b);
+            if (p.has_out) tma_load_3d(&s.Ct[st][0][0], &p.tm_C, &s.full[st], gx, t0, b);
             if (need_hand)
                 bulk_load_1d(&s.hin[st][0], p.hand + (int64_t)(c * p.K + k - 1) * PF_HAND,
                              PF_HAND * 4, &s.full[st]);

@@ -130,9 +130,14 @@ def ss_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=None, *, want_out=True,
     with torch.cuda.device(dev):
         ws_bytes = int(lib.mwc_ss_fwd_workspace_bytes(Bb, L, D, dt))
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes > 0 else None
-        rc = lib.mwc_ss_fwd(_p(u), _p(delta), _p(A), _p(B_ssm), _p(C_ssm), _p(D_ssm),
-                            _p(h_prev), _p(out), _p(h_last), _p(ckpt), _p(decay), _p(ws),
-                            ws_bytes, Bb, L, D, dt, _stream(dev))
+        if B_ssm.dim() == 4:   # grouped B / C (B, L, G, 16)
+            rc = lib.mwc_ss_fwd_grouped(_p(u), _p(delta), _p(A), _p(B_ssm), _p(C_ssm), _p(D_ssm),
+                                        _p(h_prev), _p(out), _p(h_last), _p(ckpt), _p(decay), _p(ws),
+                                        ws_bytes, Bb, L, D, B_ssm.shape[2], dt, _stream(dev))
+        else:
+            rc = lib.mwc_ss_fwd(_p(u), _p(delta), _p(A), _p(B_ssm), _p(C_ssm), _p(D_ssm),
+                                _p(h_prev), _p(out), _p(h_last), _p(ckpt), _p(decay), _p(ws),
+                                ws_bytes, Bb, L, D, dt, _stream(dev))
     _lib.check(rc, "selective_scan forward")
     _check_waits(lib, dev, "selective_scan forward")
     return out, h_last, ckpt, decay
@@ -166,10 +171,13 @@ def ss_backward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev, dout, dh_last, ckpt,
     with torch.cuda.device(dev):
         ws_bytes = int(lib.mwc_ss_bwd_workspace_bytes(Bb, L, D, dt))
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
-        rc = lib.mwc_ss_bwd(_p(u), _p(delta), _p(A), _p(B_ssm), _p(C_ssm), _p(D_ssm),
-                            _p(h_prev), _p(dout), _p(dh_last), _p(ckpt), _p(du), _p(ddelta),
-                            _p(dA), _p(dB), _p(dC), _p(dD), _p(dh_prev), _p(ws), ws_bytes,
-                            Bb, L, D, dt, _stream(dev))
+        args = (_p(u), _p(delta), _p(A), _p(B_ssm), _p(C_ssm), _p(D_ssm), _p(h_prev), _p(dout),
+                _p(dh_last), _p(ckpt), _p(du), _p(ddelta), _p(dA), _p(dB), _p(dC), _p(dD),
+                _p(dh_prev), _p(ws), ws_bytes, Bb, L, D)
+        if B_ssm.dim() == 4:   # grouped B / C: dB, dC (B, L, G, 16)
+            rc = lib.mwc_ss_bwd_grouped(*args, B_ssm.shape[2], dt, _stream(dev))
+        else:
+            rc = lib.mwc_ss_bwd(*args, dt, _stream(dev))
     _lib.check(rc, "selective_scan backward")
     _check_waits(lib, dev, "selective_scan backward")
     return du, ddelta, dA, dB, dC, dD, dh_prev
