@@ -51,6 +51,10 @@ CONFIGS = {
                  B=4, L=2048, D=5120, dtype=torch.float16, mode="fwdbwd", dist="c3", block=True,
                  metric="selective-scan block op fwd+bwd GB/s (softplus(delta+bias), y*silu(z)), "
                         "B=4 L=2048 D=5120 fp16"),
+    "c3b1": dict(workload="config 3 at batch 1 (40 (batch, 128-channel) chains, fewer than the SMs: "
+                          "the few-chain split passes of the persistent kernels)",
+                 B=1, L=2048, D=5120, dtype=torch.float16, mode="fwdbwd", dist="c3",
+                 metric="selective-scan fwd+bwd GB/s, B=1 L=2048 D=5120 fp16"),
     "conv": dict(workload="causal conv1d producer of u (width 4, SiLU) at the config-3 shape, fwd+bwd "
                           "(an addition: the reference has no conv1d)",
                  B=4, L=2048, D=5120, dtype=torch.float16, mode="conv", dist="c3",
