@@ -134,6 +134,20 @@ MWC_API int mwc_ss_bwd_grouped(const void* u, const void* delta, const void* A, 
                int64_t B, int64_t L, int64_t D, int64_t G, int dtype, void* stream);
 
 /*
+ * mwc_ss_fwd_nstate -- the forward scan of mwc_ss_fwd with N = 16, 32 or 64 states per channel:
+ * A (D, N), B_ssm / C_ssm (B, L, N), h_prev / h_last / decay (B, D, N), ckpt (B, nck, D, N).
+ * No counterpart in the reference, which supports N = 16 only (mamba_cuda.py:186-238 rejects
+ * others); the official Mamba scan takes larger N. N = 16 is mwc_ss_fwd; N = 32 / 64 run the
+ * generic forward kernels, forward only (there is no backward for them here). Workspace:
+ * mwc_ss_fwd_nstate_workspace_bytes.
+ */
+MWC_API int64_t mwc_ss_fwd_nstate_workspace_bytes(int64_t B, int64_t L, int64_t D, int64_t N, int dtype);
+MWC_API int mwc_ss_fwd_nstate(const void* u, const void* delta, const void* A, const void* Bm,
+               const void* Cm, const void* Dv, const void* h_prev, void* out, void* h_last,
+               float* ckpt, float* decay, void* workspace, int64_t workspace_bytes,
+               int64_t B, int64_t L, int64_t D, int64_t N, int dtype, void* stream);
+
+/*
  * First-order linear recurrence along axis 2 of (B, D, L, N) = (R, L, N) with R = B*D:
  * h_0 = x_0 (a_0 ignored), h_t = a_t h_{t-1} + x_t. Replaces PScan.forward /
  * parallel_scan_fn (mamba_windows_cuda/pscan.py:16-150), with the semantics of

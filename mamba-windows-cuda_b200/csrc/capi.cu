@@ -252,6 +252,63 @@ int mwc_ss_fwd_grouped(const void* u, const void* delta, const void* A, const vo
                        workspace_bytes, B, L, D, G, dtype, stream);
 }
 
+int64_t mwc_ss_fwd_nstate_workspace_bytes(int64_t B, int64_t L, int64_t D, int64_t N, int dtype) {
+    if (N == NSTATE) return mwc_ss_fwd_workspace_bytes(B, L, D, dtype);
+    if (B <= 0 || L <= 0 || D <= 0 || (N != 32 && N != 64)) return 0;
+    const FwdPlan plan = plan_fwd(B, L, D, dtype, device_sms());
+    return align_up(fwd_carry_floats(plan, B, D, (int)N) * 4, 256);
+}
+
+int mwc_ss_fwd_nstate(const void* u, const void* delta, const void* A, const void* Bm, const void* Cm,
+                      const void* Dv, const void* h_prev, void* out, void* h_last, float* ckpt,
+                      float* decay, void* workspace, int64_t workspace_bytes, int64_t B, int64_t L,
+                      int64_t D, int64_t N, int dtype, void* stream) {
+    if (N == NSTATE)
+        return ss_fwd_impl(u, delta, A, Bm, Cm, Dv, h_prev, out, h_last, ckpt, decay, workspace,
+                           workspace_bytes, B, L, D, 1, dtype, stream);
+    g_last_err_word = nullptr;
+    int rc;
+    if (N != 32 && N != 64) return fail(MWC_ERR_UNSUPPORTED, "N must be 16, 32 or 64 (got %lld)", (long long)N);
+    if ((rc = check_dtype(dtype)) != MWC_OK) return rc;
+    if ((rc = check_sizes(B, L, D)) != MWC_OK) return rc;
+    if (!u || !delta || !A || !Bm || !Cm || !Dv)
+        return fail(MWC_ERR_INVALID, "u, delta, A, B_ssm, C_ssm and D_ssm are required");
+    if (!out && !h_last && !ckpt && !decay)
+        return fail(MWC_ERR_INVALID, "no output requested");
+    if (B == 0 || D == 0) return ok();
+    // N = 32 / 64 run on the generic kernels (channel split over N / S lanes)
+    const FwdPlan plan = plan_fwd(B, L, D, dtype, device_sms());
+    const int64_t need = align_up(fwd_carry_floats(plan, B, D, (int)N) * 4, 256);
+    if (need > 0 && (!workspace || workspace_bytes < need))
+        return fail(MWC_ERR_WORKSPACE, "forward workspace of %lld bytes required, got %lld",
+                    (long long)need, (long long)workspace_bytes);
+    if (need > 0 && !aligned16(workspace))
+        return fail(MWC_ERR_WORKSPACE, "forward workspace must be 16-byte aligned");
+    const size_t es = elem_size(dtype);
+    FwdArgs a{};
+    a.u = u; a.delta = delta; a.A = A; a.Bm = Bm; a.Cm = Cm; a.Dv = Dv;
+    a.h_prev = h_prev; a.out = out; a.h_last = h_last; a.ckpt = ckpt; a.decay = decay;
+    a.carry = plan.nseg > 1 ? static_cast<float*>(workspace) : nullptr;
+    a.B = B; a.L = L; a.D = D;
+    a.seg_len = plan.seg_len; a.nseg = plan.nseg;
+    a.nck = (int)mwc_ss_ckpt_count(L);
+    a.vec = ((D * (int64_t)es) % 16 == 0) && aligned16(u) && aligned16(delta) && (!out || aligned16(out));
+    a.N = (int)N;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = launch_fwd(a, plan, dtype, s);
+    if (e != cudaSuccess) return cuda_fail(e, "selective-scan forward launch");
+    if (plan.nseg > 1) {
+        FixupArgs f{};
+        f.delta = delta; f.A = A; f.Cm = Cm; f.carry = a.carry;
+        f.out = out; f.h_last = h_last; f.decay_out = decay; f.ckpt = ckpt;
+        f.B = B; f.L = L; f.D = D; f.seg_len = plan.seg_len; f.nseg = plan.nseg;
+        f.nck = a.nck; f.mode = 0; f.vec = a.vec; f.N = (int)N;
+        e = launch_fixup(f, plan, dtype, s);
+        if (e != cudaSuccess) return cuda_fail(e, "selective-scan segment fixup launch");
+    }
+    return ok();
+}
+
 int64_t mwc_ss_bwd_workspace_bytes(int64_t B, int64_t L, int64_t D, int dtype) {
     if (B <= 0 || L <= 0 || D <= 0) return 0;
     int64_t need = bwd_ws(B, L, D, dtype).total;

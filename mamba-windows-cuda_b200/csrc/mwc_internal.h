@@ -29,6 +29,7 @@ struct FwdArgs {
     int nseg;
     int nck;
     int vec;              // 16-byte vector access of (.., D) rows is legal
+    int N;                // states per channel: 0 or 16 (the reference's N), 32, 64
 };
 
 // Carry fold + truncated fixup. mode 0: h_in for segment s = 1 + blockIdx.z is folded from
@@ -50,6 +51,7 @@ struct FixupArgs {
     int nck;
     int mode;
     int vec;
+    int N;                // states per channel: 0 or 16 (the reference's N), 32, 64
 };
 
 struct BwdArgs {
@@ -217,7 +219,7 @@ struct FwdPlan {
 };
 
 FwdPlan plan_fwd(int64_t B, int64_t L, int64_t D, int dtype, int num_sms);
-int64_t fwd_carry_floats(const FwdPlan& plan, int64_t B, int64_t D);
+int64_t fwd_carry_floats(const FwdPlan& plan, int64_t B, int64_t D, int N = 16);
 int bwd_channels_per_block(int dtype);
 
 cudaError_t launch_fwd(const FwdArgs& a, const FwdPlan& plan, int dtype, cudaStream_t s);

@@ -35,9 +35,9 @@ __device__ __forceinline__ void decay_factors(float (&a)[S], const float (&A2)[S
     }
 }
 
-template <typename T, int S, int NW>
+template <typename T, int N, int S, int NW>
 __global__ void __launch_bounds__(NW * 32) ss_fwd_kernel(const FwdArgs p) {
-    constexpr int P = NSTATE / S;   // lanes per channel
+    constexpr int P = N / S;   // lanes per channel
     constexpr int CPW = 32 / P;     // channels per warp
     constexpr int CPB = NW * CPW;   // channels per CTA
     constexpr int NT = NW * 32;
@@ -45,8 +45,8 @@ __global__ void __launch_bounds__(NW * 32) ss_fwd_kernel(const FwdArgs p) {
     __shared__ __align__(16) T su[LT][CPB];
     __shared__ __align__(16) T sd[LT][CPB];
     __shared__ __align__(16) T sy[LT][CPB];
-    __shared__ __align__(16) float sB[LT][NSTATE];
-    __shared__ __align__(16) float sC[LT][NSTATE];
+    __shared__ __align__(16) float sB[LT][N];
+    __shared__ __align__(16) float sC[LT][N];
 
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -67,21 +67,21 @@ __global__ void __launch_bounds__(NW * 32) ss_fwd_kernel(const FwdArgs p) {
     float a2max = -INFINITY;
 #pragma unroll
     for (int j = 0; j < S; ++j) {
-        A2[j] = dv ? to_f(Ap[d * NSTATE + sg * S + j]) * LOG2E : 0.f;
+        A2[j] = dv ? to_f(Ap[d * N + sg * S + j]) * LOG2E : 0.f;
         a2max = fmaxf(a2max, A2[j]);
         h[j] = 0.f;
     }
     const float Dd = dv ? to_f(static_cast<const T*>(p.Dv)[d]) : 0.f;
     if (seg == 0 && p.h_prev != nullptr && dv) {
-        const T* hp = static_cast<const T*>(p.h_prev) + (b * p.D + d) * NSTATE + sg * S;
+        const T* hp = static_cast<const T*>(p.h_prev) + (b * p.D + d) * N + sg * S;
 #pragma unroll
         for (int j = 0; j < S; ++j) h[j] = to_f(hp[j]);
     }
 
     const T* ub = static_cast<const T*>(p.u) + b * p.L * p.D + d0;
     const T* db = static_cast<const T*>(p.delta) + b * p.L * p.D + d0;
-    const T* Bb = static_cast<const T*>(p.Bm) + b * p.L * NSTATE;
-    const T* Cb = static_cast<const T*>(p.Cm) + b * p.L * NSTATE;
+    const T* Bb = static_cast<const T*>(p.Bm) + b * p.L * N;
+    const T* Cb = static_cast<const T*>(p.Cm) + b * p.L * N;
     T* yb = p.out ? static_cast<T*>(p.out) + b * p.L * p.D + d0 : nullptr;
     float sumd = 0.f;
 
@@ -90,8 +90,8 @@ __global__ void __launch_bounds__(NW * 32) ss_fwd_kernel(const FwdArgs p) {
         __syncthreads();
         load_tile<T, LT, CPB, NT>(su, ub + t0 * p.D, p.D, nrows, ncols, vec);
         load_tile<T, LT, CPB, NT>(sd, db + t0 * p.D, p.D, nrows, ncols, vec);
-        load_tile_f32<T, LT, NSTATE, NT>(sB, Bb + t0 * NSTATE, NSTATE, nrows);
-        if (yb) load_tile_f32<T, LT, NSTATE, NT>(sC, Cb + t0 * NSTATE, NSTATE, nrows);
+        load_tile_f32<T, LT, N, NT>(sB, Bb + t0 * N, N, nrows);
+        if (yb) load_tile_f32<T, LT, N, NT>(sC, Cb + t0 * N, N, nrows);
         __syncthreads();
         // Rows past the end are zero-filled: delta = 0 gives a = 1 and no input, so the
         // state is unchanged and no per-step bound check is needed.
@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(NW * 32) ss_fwd_kernel(const FwdArgs p) {
             if ((i + 1) % CK == 0 && p.ckpt != nullptr) {
                 const int64_t k = (t0 + i + 1) / CK - 1;
                 if (k < p.nck && dv) {
-                    float* c = p.ckpt + ((b * p.nck + k) * p.D + d) * NSTATE + sg * S;
+                    float* c = p.ckpt + ((b * p.nck + k) * p.D + d) * N + sg * S;
 #pragma unroll
                     for (int j = 0; j < S; ++j) c[j] = h[j];
                 }
@@ -132,34 +132,34 @@ __global__ void __launch_bounds__(NW * 32) ss_fwd_kernel(const FwdArgs p) {
     if (!dv) return;
     if (p.nseg == 1) {
         if (p.h_last != nullptr) {
-            T* hl = static_cast<T*>(p.h_last) + (b * p.D + d) * NSTATE + sg * S;
+            T* hl = static_cast<T*>(p.h_last) + (b * p.D + d) * N + sg * S;
 #pragma unroll
             for (int j = 0; j < S; ++j) hl[j] = from_f<T>(h[j]);
         }
         if (p.decay != nullptr) {
-            float* dc = p.decay + (b * p.D + d) * NSTATE + sg * S;
+            float* dc = p.decay + (b * p.D + d) * N + sg * S;
 #pragma unroll
             for (int j = 0; j < S; ++j) dc[j] = ex2(fminf(A2[j] * sumd, ARG2_HI));
         }
     } else {
-        float* c = p.carry + ((b * p.nseg + seg) * p.D + d) * (NSTATE + 1);
+        float* c = p.carry + ((b * p.nseg + seg) * p.D + d) * (N + 1);
 #pragma unroll
         for (int j = 0; j < S; ++j) c[sg * S + j] = h[j];
-        if (sg == 0) c[NSTATE] = sumd;
+        if (sg == 0) c[N] = sumd;
     }
 }
 
 // Carry fold + truncated fixup of a segment that was scanned from zero.
-template <typename T, int S, int NW>
+template <typename T, int N, int S, int NW>
 __global__ void __launch_bounds__(NW * 32) ss_fixup_kernel(const FixupArgs p) {
-    constexpr int P = NSTATE / S;
+    constexpr int P = N / S;
     constexpr int CPW = 32 / P;
     constexpr int CPB = NW * CPW;
     constexpr int NT = NW * 32;
     constexpr int LT = FWD_LT;
     __shared__ __align__(16) T sd[LT][CPB];
     __shared__ __align__(16) T sy[LT][CPB];
-    __shared__ __align__(16) float sC[LT][NSTATE];
+    __shared__ __align__(16) float sC[LT][N];
 
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -181,7 +181,7 @@ __global__ void __launch_bounds__(NW * 32) ss_fixup_kernel(const FixupArgs p) {
     float a2max = -INFINITY;
 #pragma unroll
     for (int j = 0; j < S; ++j) {
-        A2[j] = dv ? to_f(Ap[d * NSTATE + sg * S + j]) * LOG2E : 0.f;
+        A2[j] = dv ? to_f(Ap[d * N + sg * S + j]) * LOG2E : 0.f;
         a2max = fmaxf(a2max, A2[j]);
         hin[j] = 0.f;
     }
@@ -190,37 +190,37 @@ __global__ void __launch_bounds__(NW * 32) ss_fixup_kernel(const FixupArgs p) {
         if (p.mode == 0) {
             // h_in(seg) = fold over earlier segments of (decay_s, S_s): h <- decay_s h + S_s
             for (int s = 0; s < seg; ++s) {
-                const float* c = p.carry + ((b * p.nseg + s) * p.D + d) * (NSTATE + 1);
-                const float sds = c[NSTATE];
+                const float* c = p.carry + ((b * p.nseg + s) * p.D + d) * (N + 1);
+                const float sds = c[N];
 #pragma unroll
                 for (int j = 0; j < S; ++j)
                     hin[j] = fmaf(ex2(fminf(A2[j] * sds, ARG2_HI)), hin[j], c[sg * S + j]);
             }
             if (last) {
-                const float* c = p.carry + ((b * p.nseg + seg) * p.D + d) * (NSTATE + 1);
+                const float* c = p.carry + ((b * p.nseg + seg) * p.D + d) * (N + 1);
                 if (p.h_last != nullptr) {
-                    T* hl = static_cast<T*>(p.h_last) + (b * p.D + d) * NSTATE + sg * S;
+                    T* hl = static_cast<T*>(p.h_last) + (b * p.D + d) * N + sg * S;
 #pragma unroll
                     for (int j = 0; j < S; ++j)
-                        hl[j] = from_f<T>(fmaf(ex2(fminf(A2[j] * c[NSTATE], ARG2_HI)), hin[j],
+                        hl[j] = from_f<T>(fmaf(ex2(fminf(A2[j] * c[N], ARG2_HI)), hin[j],
                                                c[sg * S + j]));
                 }
                 if (p.decay_out != nullptr) {
                     float tot = 0.f;
                     for (int s = 0; s < p.nseg; ++s)
-                        tot += p.carry[((b * p.nseg + s) * p.D + d) * (NSTATE + 1) + NSTATE];
-                    float* dc = p.decay_out + (b * p.D + d) * NSTATE + sg * S;
+                        tot += p.carry[((b * p.nseg + s) * p.D + d) * (N + 1) + N];
+                    float* dc = p.decay_out + (b * p.D + d) * N + sg * S;
 #pragma unroll
                     for (int j = 0; j < S; ++j) dc[j] = ex2(fminf(A2[j] * tot, ARG2_HI));
                 }
             }
         } else {
-            const float* hi = p.h_in + (b * p.D + d) * NSTATE + sg * S;
+            const float* hi = p.h_in + (b * p.D + d) * N + sg * S;
 #pragma unroll
             for (int j = 0; j < S; ++j) hin[j] = hi[j];
             if (p.h_last != nullptr) {
-                T* hl = static_cast<T*>(p.h_last) + (b * p.D + d) * NSTATE + sg * S;
-                const float* dc = p.decay + (b * p.D + d) * NSTATE + sg * S;
+                T* hl = static_cast<T*>(p.h_last) + (b * p.D + d) * N + sg * S;
+                const float* dc = p.decay + (b * p.D + d) * N + sg * S;
 #pragma unroll
                 for (int j = 0; j < S; ++j) hl[j] = from_f<T>(fmaf(dc[j], hin[j], to_f(hl[j])));
             }
@@ -229,7 +229,7 @@ __global__ void __launch_bounds__(NW * 32) ss_fixup_kernel(const FixupArgs p) {
     if (p.out == nullptr && p.ckpt == nullptr) return;
 
     const T* db = static_cast<const T*>(p.delta) + b * p.L * p.D + d0;
-    const T* Cb = static_cast<const T*>(p.Cm) + b * p.L * NSTATE;
+    const T* Cb = static_cast<const T*>(p.Cm) + b * p.L * N;
     T* yb = p.out ? static_cast<T*>(p.out) + b * p.L * p.D + d0 : nullptr;
     float cum = 0.f;
     bool neg = false;
@@ -239,7 +239,7 @@ __global__ void __launch_bounds__(NW * 32) ss_fixup_kernel(const FixupArgs p) {
         load_tile<T, LT, CPB, NT>(sd, db + t0 * p.D, p.D, nrows, ncols, vec);
         if (yb) {
             load_tile<T, LT, CPB, NT>(sy, yb + t0 * p.D, p.D, nrows, ncols, vec);
-            load_tile_f32<T, LT, NSTATE, NT>(sC, Cb + t0 * NSTATE, NSTATE, nrows);
+            load_tile_f32<T, LT, N, NT>(sC, Cb + t0 * N, N, nrows);
         }
         __syncthreads();
 #pragma unroll
@@ -261,7 +261,7 @@ __global__ void __launch_bounds__(NW * 32) ss_fixup_kernel(const FixupArgs p) {
             if ((i + 1) % CK == 0 && p.ckpt != nullptr) {
                 const int64_t k = (t0 + i + 1) / CK - 1;
                 if (k < p.nck && dv) {
-                    float* c = p.ckpt + ((b * p.nck + k) * p.D + d) * NSTATE + sg * S;
+                    float* c = p.ckpt + ((b * p.nck + k) * p.D + d) * N + sg * S;
 #pragma unroll
                     for (int j = 0; j < S; ++j) c[j] += corr[j];
                 }
@@ -304,44 +304,59 @@ FwdPlan plan_fwd(int64_t B, int64_t L, int64_t D, int dtype, int num_sms) {
     return plan;
 }
 
-int64_t fwd_carry_floats(const FwdPlan& plan, int64_t B, int64_t D) {
-    return plan.nseg > 1 ? B * plan.nseg * D * (NSTATE + 1) : 0;
+int64_t fwd_carry_floats(const FwdPlan& plan, int64_t B, int64_t D, int N) {
+    return plan.nseg > 1 ? B * plan.nseg * D * (N + 1) : 0;
 }
 
-template <typename T, int S>
+template <typename T, int N, int S>
 static cudaError_t launch_fwd_t(const FwdArgs& a, const FwdPlan& plan, cudaStream_t s) {
-    constexpr int CPB = FWD_NW * (32 / (NSTATE / S));
+    constexpr int CPB = FWD_NW * (32 / (N / S));
     dim3 grid((unsigned)((a.D + CPB - 1) / CPB), (unsigned)a.B, (unsigned)plan.nseg);
-    ss_fwd_kernel<T, S, FWD_NW><<<grid, FWD_NW * 32, 0, s>>>(a);
+    ss_fwd_kernel<T, N, S, FWD_NW><<<grid, FWD_NW * 32, 0, s>>>(a);
     return cudaGetLastError();
 }
 
-template <typename T, int S>
+template <typename T, int N, int S>
 static cudaError_t launch_fixup_t(const FixupArgs& a, const FwdPlan& plan, cudaStream_t s) {
-    constexpr int CPB = FWD_NW * (32 / (NSTATE / S));
+    constexpr int CPB = FWD_NW * (32 / (N / S));
     const unsigned gz = a.mode == 0 ? (unsigned)(plan.nseg - 1) : 1u;
     if (gz == 0) return cudaSuccess;
     dim3 grid((unsigned)((a.D + CPB - 1) / CPB), (unsigned)a.B, gz);
-    ss_fixup_kernel<T, S, FWD_NW><<<grid, FWD_NW * 32, 0, s>>>(a);
+    ss_fixup_kernel<T, N, S, FWD_NW><<<grid, FWD_NW * 32, 0, s>>>(a);
     return cudaGetLastError();
+}
+
+// states per channel: 16 (the reference's N; also what N = 0 in the args means), 32 or 64
+template <typename T, int N>
+static cudaError_t launch_fwd_n(const FwdArgs& a, const FwdPlan& plan, cudaStream_t s) {
+    switch (plan.states_per_thread) {
+        case 16: return launch_fwd_t<T, N, 16>(a, plan, s);
+        case 8: return launch_fwd_t<T, N, 8>(a, plan, s);
+        default: return launch_fwd_t<T, N, 4>(a, plan, s);
+    }
 }
 
 template <typename T>
 static cudaError_t launch_fwd_s(const FwdArgs& a, const FwdPlan& plan, cudaStream_t s) {
+    if (a.N == 64) return launch_fwd_n<T, 64>(a, plan, s);
+    if (a.N == 32) return launch_fwd_n<T, 32>(a, plan, s);
+    return launch_fwd_n<T, NSTATE>(a, plan, s);
+}
+
+template <typename T, int N>
+static cudaError_t launch_fixup_n(const FixupArgs& a, const FwdPlan& plan, cudaStream_t s) {
     switch (plan.states_per_thread) {
-        case 16: return launch_fwd_t<T, 16>(a, plan, s);
-        case 8: return launch_fwd_t<T, 8>(a, plan, s);
-        default: return launch_fwd_t<T, 4>(a, plan, s);
+        case 16: return launch_fixup_t<T, N, 16>(a, plan, s);
+        case 8: return launch_fixup_t<T, N, 8>(a, plan, s);
+        default: return launch_fixup_t<T, N, 4>(a, plan, s);
     }
 }
 
 template <typename T>
 static cudaError_t launch_fixup_s(const FixupArgs& a, const FwdPlan& plan, cudaStream_t s) {
-    switch (plan.states_per_thread) {
-        case 16: return launch_fixup_t<T, 16>(a, plan, s);
-        case 8: return launch_fixup_t<T, 8>(a, plan, s);
-        default: return launch_fixup_t<T, 4>(a, plan, s);
-    }
+    if (a.N == 64) return launch_fixup_n<T, 64>(a, plan, s);
+    if (a.N == 32) return launch_fixup_n<T, 32>(a, plan, s);
+    return launch_fixup_n<T, NSTATE>(a, plan, s);
 }
 
 cudaError_t launch_fwd(const FwdArgs& a, const FwdPlan& plan, int dtype, cudaStream_t s) {

@@ -112,12 +112,13 @@ def ss_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=None, *, want_out=True,
     Returns (out, h_last, ckpt, decay); entries not requested are None.
     """
     Bb, L, D = u.shape
+    N = A.shape[1]   # 16 everywhere except the N = 32 / 64 forward (mwc_ss_fwd_nstate)
     dev = u.device
     out = torch.empty_like(u) if want_out else None
-    h_last = torch.empty((Bb, D, NSTATE), dtype=u.dtype, device=dev) if want_h_last else None
-    ckpt = (torch.empty((Bb, ckpt_count(L), D, NSTATE), dtype=torch.float32, device=dev)
+    h_last = torch.empty((Bb, D, N), dtype=u.dtype, device=dev) if want_h_last else None
+    ckpt = (torch.empty((Bb, ckpt_count(L), D, N), dtype=torch.float32, device=dev)
             if want_ckpt else None)
-    decay = (torch.empty((Bb, D, NSTATE), dtype=torch.float32, device=dev)
+    decay = (torch.empty((Bb, D, N), dtype=torch.float32, device=dev)
              if want_decay else None)
     if L == 0 or Bb == 0 or D == 0:
         if h_last is not None:
@@ -128,9 +129,16 @@ def ss_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=None, *, want_out=True,
     lib = _lib.load()
     dt = dtype_code(u)
     with torch.cuda.device(dev):
-        ws_bytes = int(lib.mwc_ss_fwd_workspace_bytes(Bb, L, D, dt))
+        if N != NSTATE:
+            ws_bytes = int(lib.mwc_ss_fwd_nstate_workspace_bytes(Bb, L, D, N, dt))
+        else:
+            ws_bytes = int(lib.mwc_ss_fwd_workspace_bytes(Bb, L, D, dt))
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes > 0 else None
-        if B_ssm.dim() == 4:   # grouped B / C (B, L, G, 16)
+        if N != NSTATE:
+            rc = lib.mwc_ss_fwd_nstate(_p(u), _p(delta), _p(A), _p(B_ssm), _p(C_ssm), _p(D_ssm),
+                                       _p(h_prev), _p(out), _p(h_last), _p(ckpt), _p(decay), _p(ws),
+                                       ws_bytes, Bb, L, D, N, dt, _stream(dev))
+        elif B_ssm.dim() == 4:   # grouped B / C (B, L, G, 16)
             rc = lib.mwc_ss_fwd_grouped(_p(u), _p(delta), _p(A), _p(B_ssm), _p(C_ssm), _p(D_ssm),
                                         _p(h_prev), _p(out), _p(h_last), _p(ckpt), _p(decay), _p(ws),
                                         ws_bytes, Bb, L, D, B_ssm.shape[2], dt, _stream(dev))
