@@ -3,10 +3,11 @@
 // 16 steps for the backward, and the L-segmented mode (segment scans from zero + carry
 // fold + truncated fixup) used when batch x channels cannot fill the GPU.
 //
-// Thread layout: a channel's 16 states are split over P = 16/S lanes (S states each, held
-// in registers). Lanes of one warp cover 32/P channels, consecutive lanes consecutive
-// channels, so the (B, L, D) tiles are read and written along D. Tiles of u / delta
-// (LT x channels) and the B / C rows (LT x 16, float32) are staged in shared memory.
+// Thread layout: a channel's N states (N = 16, the reference's; 32 / 64 for the forward of
+// mwc_ss_fwd_nstate) are split over P = N/S lanes (S states each, held in registers). Lanes
+// of one warp cover 32/P channels, consecutive lanes consecutive channels, so the (B, L, D)
+// tiles are read and written along D. Tiles of u / delta (LT x channels) and the B / C rows
+// (LT x N, float32) are staged in shared memory.
 //
 // Reference semantics: selective_scan_fwd_kernel_v4 (mamba_windows_cuda/mamba_cuda.py:93-174)
 // and selective_scan_fwd_store_kernel (:611-667): a = safe_exp(delta*A) with the exponent
