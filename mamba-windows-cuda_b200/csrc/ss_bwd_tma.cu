@@ -797,9 +797,10 @@ __global__ void ss_bwd_persistent_final_kernel(const __grid_constant__ PBwdArgs 
 // adjoint state at the segment's start when q = 0 at its end (dh_last for the last segment):
 //   q <- a_t (dout_t C_t + q),  a_t = 2^(delta_t A log2 e)   (the reference's adjoint without
 // the gradient terms, mamba_windows_cuda/mamba_cuda.py:703-742), and the segment's delta sum.
-// Thread = (channel, half): 8 of the channel's 16 states; the CTA stages 32-step tiles of
-// delta / dout (32 x 128, 16-byte vectors: rows of D * elem are 16-byte multiples on this
-// path) and C (32 x 16, float32) in shared memory.
+// Thread = (channel, half): 8 of the channel's 16 states as packed float2 pairs; the CTA
+// stages 32-step tiles of delta / dout (32 x 128, 16-byte vectors: rows of D * elem are
+// 16-byte multiples on this path) and C (32 x 16, float32) in shared memory, each thread
+// loading its share of the next tile into registers while the current one is computed.
 constexpr int AJ_LT = 32;
 
 template <typename T>
@@ -822,56 +823,110 @@ __global__ void __launch_bounds__(256) ss_bwd_adjoint_kernel(
     const int ch = w * 16 + (lane >> 1), n0 = (lane & 1) * 8;
     const int64_t d = (int64_t)blk * PB_CPB + ch;
     const bool dv = d < D;
-    float A2[8], q[8];
+    float2 A2[4], q[4];
+    bool a_nonpos = true;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        A2[j] = dv ? to_f(A[d * NSTATE + n0 + j]) * LOG2E : 0.f;
-        q[j] = (kp == 0 && dh_last != nullptr && dv) ? to_f(dh_last[((int64_t)b * D + d) * NSTATE + n0 + j]) : 0.f;
+    for (int j = 0; j < 4; ++j) {
+        float av[2], qv[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const int n = n0 + 2 * j + e;
+            av[e] = dv ? to_f(A[d * NSTATE + n]) * LOG2E : 0.f;
+            qv[e] = (kp == 0 && dh_last != nullptr && dv) ? to_f(dh_last[((int64_t)b * D + d) * NSTATE + n]) : 0.f;
+            a_nonpos = a_nonpos && av[e] <= 0.f;
+        }
+        A2[j] = make_float2(av[0], av[1]);
+        q[j] = make_float2(qv[0], qv[1]);
     }
     float sumd = 0.f;
     const int ntl = (tend - tstart + AJ_LT - 1) / AJ_LT;
+    // This thread's share of a tile, loaded into registers one tile ahead (the next tile's
+    // loads are in flight while the current one is computed).
+    constexpr int NV = AJ_LT * VPR / 256;       // 16-byte vectors per tensor and thread
+    constexpr int NCE = AJ_LT * NSTATE / 256;   // C elements per thread
+    static_assert(AJ_LT * VPR % 256 == 0 && AJ_LT * NSTATE % 256 == 0, "whole tiles per CTA");
+    uint4 ra[NV], rg[NV];
+    float rc[NCE];
+    bool rneg = false;   // a delta of the prefetched share has its sign bit set
+    auto fetch = [&](int ti) {
+        const int t0 = tstart + ti * AJ_LT;
+        const int nr = min(AJ_LT, tend - t0);
+        rneg = false;
+#pragma unroll
+        for (int v = 0; v < NV; ++v) {
+            const int idx = tid + v * 256, r = idx / VPR, col = idx % VPR;
+            const int64_t dd = (int64_t)blk * PB_CPB + col * VE;
+            ra[v] = make_uint4(0u, 0u, 0u, 0u);
+            rg[v] = ra[v];
+            if (r < nr && dd < D) {
+                const int64_t off = ((int64_t)b * L + t0 + r) * D + dd;
+                ra[v] = *reinterpret_cast<const uint4*>(delta + off);
+                rg[v] = *reinterpret_cast<const uint4*>(dout + off);
+            }
+            constexpr uint32_t SIGN = sizeof(T) == 2 ? 0x80008000u : 0x80000000u;
+            rneg = rneg || (((ra[v].x | ra[v].y | ra[v].z | ra[v].w) & SIGN) != 0u);
+        }
+#pragma unroll
+        for (int e = 0; e < NCE; ++e) {
+            const int idx = tid + e * 256, r = idx / NSTATE, n = idx % NSTATE;
+            rc[e] = r < nr ? to_f(Cm[(((int64_t)b * L + t0 + r) * G + grp) * NSTATE + n]) : 0.f;
+        }
+    };
+    if (ntl > 0) fetch(ntl - 1);
     for (int ti = ntl - 1; ti >= 0; --ti) {
         const int t0 = tstart + ti * AJ_LT;
         const int nr = min(AJ_LT, tend - t0);
         __syncthreads();   // the previous tile is no longer read
-        for (int idx = tid; idx < AJ_LT * VPR; idx += 256) {
-            const int r = idx / VPR, v = idx % VPR;
-            const int64_t dd = (int64_t)blk * PB_CPB + v * VE;
-            uint4 a4 = make_uint4(0u, 0u, 0u, 0u), g4 = a4;
-            if (r < nr && dd < D) {
-                const int64_t off = ((int64_t)b * L + t0 + r) * D + dd;
-                a4 = *reinterpret_cast<const uint4*>(delta + off);
-                g4 = *reinterpret_cast<const uint4*>(dout + off);
-            }
-            *reinterpret_cast<uint4*>(&sd[r][v * VE]) = a4;
-            *reinterpret_cast<uint4*>(&sgy[r][v * VE]) = g4;
+#pragma unroll
+        for (int v = 0; v < NV; ++v) {
+            const int idx = tid + v * 256, r = idx / VPR, col = idx % VPR;
+            *reinterpret_cast<uint4*>(&sd[r][col * VE]) = ra[v];
+            *reinterpret_cast<uint4*>(&sgy[r][col * VE]) = rg[v];
         }
-        for (int idx = tid; idx < AJ_LT * NSTATE; idx += 256) {
-            const int r = idx / NSTATE, n = idx % NSTATE;
-            sC[r][n] = r < nr ? to_f(Cm[(((int64_t)b * L + t0 + r) * G + grp) * NSTATE + n]) : 0.f;
+#pragma unroll
+        for (int e = 0; e < NCE; ++e) {
+            const int idx = tid + e * 256;
+            sC[idx / NSTATE][idx % NSTATE] = rc[e];
         }
-        __syncthreads();
+        // the tile is in shared memory; the exponent clamp is the identity for the whole tile
+        // when no delta of it is negative and A <= 0 for every channel of the CTA
+        const bool noclamp = __syncthreads_and(!rneg && a_nonpos) != 0;
+        if (ti > 0) fetch(ti - 1);
+        auto steps = [&](auto clamp_tag) {
+            constexpr bool CLAMP = decltype(clamp_tag)::value;
 #pragma unroll 4
-        for (int r = nr - 1; r >= 0; --r) {
-            const float dt = to_f(sd[r][ch]), gy = to_f(sgy[r][ch]);
-            sumd += dt;
-            const float4* Cq = reinterpret_cast<const float4*>(&sC[r][n0]);
+            for (int r = nr - 1; r >= 0; --r) {
+                const float dt = to_f(sd[r][ch]), gy = to_f(sgy[r][ch]);
+                sumd += dt;
+                const float2 dt2 = make_float2(dt, dt), gy2 = make_float2(gy, gy);
+                const float4* Cq = reinterpret_cast<const float4*>(&sC[r][n0]);
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const float4 c4 = Cq[h];
-                const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
+                for (int h = 0; h < 2; ++h) {
+                    const float4 c4 = Cq[h];
+                    const float2 cp[2] = {make_float2(c4.x, c4.y), make_float2(c4.z, c4.w)};
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int jj = 4 * h + j;
-                    const float a = ex2(fminf(dt * A2[jj], ARG2_HI));
-                    q[jj] = a * fmaf(gy, cv[j], q[jj]);
+                    for (int j = 0; j < 2; ++j) {
+                        const int jj = 2 * h + j;
+                        float2 x = __fmul2_rn(dt2, A2[jj]);
+                        if constexpr (CLAMP) x = make_float2(fminf(x.x, ARG2_HI), fminf(x.y, ARG2_HI));
+                        const float2 a = make_float2(ex2(x.x), ex2(x.y));
+                        q[jj] = __fmul2_rn(a, __ffma2_rn(gy2, cp[j], q[jj]));
+                    }
                 }
             }
-        }
+        };
+        if (noclamp) steps(std::false_type{});
+        else steps(std::true_type{});
+    }
+    float qs[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        qs[2 * j] = q[j].x;
+        qs[2 * j + 1] = q[j].y;
     }
     float* rec = hand + ((int64_t)(c * K + kp) * PB_CPB + ch) * NSTATE + n0;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) rec[j] = q[j];
+    for (int j = 0; j < 8; ++j) rec[j] = qs[j];
     if ((lane & 1) == 0) segsum[(int64_t)(c * K + kp) * PB_CPB + ch] = sumd;
 }
 
