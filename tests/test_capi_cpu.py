@@ -112,6 +112,29 @@ def test_python_api_rejects_cpu_tensors_like_the_reference():
         m.parallel_scan_fn(torch.rand(1, 2, 8, 1), torch.rand(1, 2, 8, 1))
 
 
+def test_added_python_apis_reject_cpu_tensors():
+    from mamba_windows_cuda.grouped import selective_scan_grouped
+    from mamba_windows_cuda.nstate import selective_scan_forward_nstate
+    x = make_inputs(1, 8, 4)
+    args = [x[k] for k in ("u", "delta", "A", "Bm", "Cm", "Dv")]
+    with pytest.raises(RuntimeError, match="CUDA tensor"):
+        selective_scan_grouped(*args[:3], x["Bm"].unsqueeze(2), x["Cm"].unsqueeze(2), args[5])
+    with pytest.raises(RuntimeError, match="CUDA tensors"), torch.no_grad():
+        selective_scan_forward_nstate(*args)
+
+
+def test_nstate_workspace_query(lib):
+    # N = 32 / 64: the generic forward's segment carries (N + 1 floats per channel and segment)
+    # for a long sequence over few channels, none for a short one; other N: none
+    assert lib.mwc_ss_fwd_nstate_workspace_bytes(1, 65536, 64, 32, 0) > 0
+    assert lib.mwc_ss_fwd_nstate_workspace_bytes(1, 65536, 64, 64, 0) > \
+        lib.mwc_ss_fwd_nstate_workspace_bytes(1, 65536, 64, 32, 0)
+    assert lib.mwc_ss_fwd_nstate_workspace_bytes(1, 256, 64, 32, 0) == 0
+    assert lib.mwc_ss_fwd_nstate_workspace_bytes(1, 65536, 64, 48, 0) == 0
+    assert lib.mwc_ss_fwd_nstate_workspace_bytes(4, 2048, 5120, 16, 1) == \
+        lib.mwc_ss_fwd_workspace_bytes(4, 2048, 5120, 1)
+
+
 def test_selective_scan_ref_and_backward_match_oracle():
     from mamba_windows_cuda.mamba_cuda import selective_scan_backward, selective_scan_ref
     x = make_inputs(2, 40, 12, torch.float64, seed=4, with_state=True)
