@@ -158,7 +158,7 @@ struct PBwdArgs {
     float* hand;     // (chains, K, 128, 16): adjoint state handed to the previous segment
     float* ws_a;     // (units, 128, 16) dA partial sums
     float* ws_d;     // (units, 128) dD partial sums
-    float* ws_bc;    // (blocks, B, nck*16, 32) dB | dC partial sums
+    float* ws_bc;    // (B, nck*16, blocks, 32) dB | dC partial sums
     int* flags;
     int* counter;
     int* err;

@@ -330,7 +330,9 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
             if (it > 0) {
                 const int rb = (it - 1) % RB;
                 mbar_wait(&s.redfull[rb], (unsigned)((it - 1) / RB) & 1u, p.err);
-                float* wb = p.ws_bc + (((int64_t)pblk * p.B + pb) * Lp + pt0) * (2 * NSTATE);
+                // partials laid out (b, t, block, 32): the finalize reads a (b, t) row's blocks
+                // as one contiguous run
+                float* wb = p.ws_bc + (((int64_t)pb * Lp + pt0) * p.nblk + pblk) * (2 * NSTATE);
 #pragma unroll 4
                 for (int r = 0; r < (PB_LT * 2 * NSTATE) / 32; ++r) {
                     const int idx = lane + r * 32;
@@ -338,7 +340,7 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                     float acc = s.red[rb][0][i][vv];
 #pragma unroll
                     for (int ww = 1; ww < PB_NCW; ++ww) acc += s.red[rb][ww][i][vv];
-                    wb[idx] = acc;
+                    wb[(int64_t)i * p.nblk * (2 * NSTATE) + vv] = acc;
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive_b(&s.redempty[rb]);
@@ -771,7 +773,7 @@ __global__ void ss_bwd_persistent_final_kernel(const __grid_constant__ PBwdArgs 
             const int64_t b = bt / p.L, t = bt % p.L;
             float s = 0.f;
             for (int blk = g * bpg; blk < (g + 1) * bpg; ++blk)
-                s += p.ws_bc[(((int64_t)blk * p.B + b) * Lp + t) * (2 * NSTATE) + v];
+                s += p.ws_bc[(((int64_t)b * Lp + t) * p.nblk + blk) * (2 * NSTATE) + v];
             if (v < NSTATE) dB[btg * NSTATE + v] = from_f<T>(s);
             else dC[btg * NSTATE + v - NSTATE] = from_f<T>(s);
         } else {
