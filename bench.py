@@ -79,7 +79,7 @@ CONFIGS = {
 # DRAM bytes (read + write) of one launch of the dominant kernel, from one ncu capture of
 # this bench's own command (profiles/ss_fwd_bwd_persistent_c3_fp16.md).
 CAPTURED_TRAFFIC = {
-    "c3": {"bytes": 419.029248e6 + 204.617216e6,
+    "c3": {"bytes": 419.284992e6 + 204.703744e6,
            "source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, ss_bwd_persistent_kernel, "
                      "profiles/ss_fwd_bwd_persistent_c3_fp16.md"},
     "conv": {"bytes": 167.935232e6 + 54.496256e6,
