@@ -55,6 +55,14 @@ CONFIGS = {
                           "the few-chain split passes of the persistent kernels)",
                  B=1, L=2048, D=5120, dtype=torch.float16, mode="fwdbwd", dist="c3",
                  metric="selective-scan fwd+bwd GB/s, B=1 L=2048 D=5120 fp16"),
+    "c3g4": dict(workload="config 3 shape with grouped B / C, G = 4 (B, C of shape (4, 2048, 4, 16); "
+                          "an addition: the reference's B / C are one group)",
+                 B=4, L=2048, D=5120, dtype=torch.float16, mode="fwdbwd", dist="c3", groups=4,
+                 metric="selective-scan fwd+bwd GB/s, B=4 L=2048 D=5120 G=4 fp16"),
+    "c3n32": dict(workload="config 3 shape with N = 32 states per channel (selective_scan_nstate: two "
+                           "16-state slices; an addition: the reference supports N = 16 only)",
+                  B=4, L=2048, D=5120, dtype=torch.float16, mode="fwdbwd", dist="c3", nstate=32,
+                  metric="selective-scan fwd+bwd GB/s, B=4 L=2048 D=5120 N=32 fp16"),
     "conv": dict(workload="causal conv1d producer of u (width 4, SiLU) at the config-3 shape, fwd+bwd "
                           "(an addition: the reference has no conv1d)",
                  B=4, L=2048, D=5120, dtype=torch.float16, mode="conv", dist="c3",
@@ -265,6 +273,11 @@ def oracle_sample(cfg, target_s, seed=0):
             O.lin_fwd(a, x)
             return time.perf_counter() - t0
         (u, delta, A, Bm, Cm, Dv), gy = make_ss_inputs(cfg, "cpu", seed, L=Ls)
+        nst = cfg.get("nstate", NSTATE)
+        if nst != NSTATE:   # the N-state workload: A = -(n+1) for n < N, B / C (B, L, N)
+            g = torch.Generator().manual_seed(seed + 1)
+            A = -torch.arange(1, nst + 1, dtype=torch.float64).repeat(D, 1)
+            Bm, Cm = torch.randn(B, Ls, nst, generator=g), torch.randn(B, Ls, nst, generator=g)
         n = [t.double().numpy() for t in (u, delta, A, Bm, Cm, Dv)]
         t0 = time.perf_counter()
         O.ss_fwd(*n)
@@ -342,6 +355,7 @@ def bench_fwdbwd(args, cfg, dev, world, rank, peaks):
     ins, gy = make_ss_inputs(cfg, dev, seed=1000 + rank)
     es = ins[0].element_size()
     block = cfg.get("block", False)
+    nst = cfg.get("nstate", NSTATE)   # states per channel (16 except the N-state config)
     if block:
         # block form: delta is the pre-activation, plus z (B, L, D) and delta_bias (D)
         from mamba_windows_cuda.selective_scan_interface import selective_scan_fn
@@ -352,6 +366,21 @@ def bench_fwdbwd(args, cfg, dev, world, rank, peaks):
 
         def mod(*a):
             return selective_scan_fn(*a[:6], z=a[6], delta_bias=a[7], delta_softplus=True)
+    elif cfg.get("groups", 1) > 1:
+        # grouped B / C (B, L, G, 16): channel d reads group d // (D // G)
+        from mamba_windows_cuda.grouped import selective_scan_grouped
+        gen = torch.Generator(device=dev).manual_seed(2000 + rank)
+        ins[3], ins[4] = [torch.randn(B, L, cfg["groups"], NSTATE, generator=gen, device=dev).to(cfg["dtype"])
+                          for _ in range(2)]
+        mod = selective_scan_grouped
+    elif nst != NSTATE:
+        # N states per channel: A = -(n+1) for n < N, B / C (B, L, N); N / 16 slices of 16 states
+        from mamba_windows_cuda.nstate import selective_scan_nstate
+        gen = torch.Generator(device=dev).manual_seed(2000 + rank)
+        n1 = torch.arange(1, nst + 1, dtype=torch.float32, device=dev)
+        ins[2] = (-n1.repeat(D, 1)).to(cfg["dtype"])
+        ins[3], ins[4] = [torch.randn(B, L, nst, generator=gen, device=dev).to(cfg["dtype"]) for _ in range(2)]
+        mod = selective_scan_nstate
     else:
         mod = mwc.SelectiveScanCuda()
     leaves = [t.clone().requires_grad_(True) for t in ins]
@@ -393,12 +422,12 @@ def bench_fwdbwd(args, cfg, dev, world, rank, peaks):
     # backward scan + its finalize; the block form adds the delta transform and the gate in
     # both directions and the ddelta / dbias pair
     fk, bk = scan_launches(B, L, D, es, dev)
-    launches_per_step = fk + bk + (6 if block else 0)
+    launches_per_step = (fk + bk) * (nst // NSTATE) + (6 if block else 0)
 
     # roofline of the dominant kernel (the backward: reverse scan + its fixed-order reduction)
     mufu_peak = 148 * 16 * peaks["sm_max_mhz"] * 1e6  # ex2 / s at the max SM clock
     E = B * L * D
-    bwd_bytes = ss_bytes(B, L, D, es, "fwdbwd") - ss_bytes(B, L, D, es, "fwd") + 2 * B * D * NSTATE * es
+    bwd_bytes = ss_bytes(B, L, D, es, "fwdbwd") - ss_bytes(B, L, D, es, "fwd") + 2 * B * D * nst * es
     fwd_bytes = nbytes - bwd_bytes
 
     def roof(nb, nex2, t_ms):
@@ -407,8 +436,8 @@ def bench_fwdbwd(args, cfg, dev, world, rank, peaks):
                     ex2_per_s=nex2 / t, mufu_frac=nex2 / t / mufu_peak,
                     frac=max(nb / (peaks["hbm_gbs"] * 1e9), nex2 / mufu_peak) / t)
 
-    rb = roof(bwd_bytes, 16 * E, bwd_ms)
-    rf = roof(fwd_bytes, 16 * E, fwd_ms)
+    rb = roof(bwd_bytes, nst * E, bwd_ms)   # one ex2 per element and state in each pass
+    rf = roof(fwd_bytes, nst * E, fwd_ms)
     rs = roof(nbytes, 32 * E, ms / args.steps)
     traffic = CAPTURED_TRAFFIC.get(args.config)
     roofline = {
@@ -419,7 +448,7 @@ def bench_fwdbwd(args, cfg, dev, world, rank, peaks):
         "traffic_source": traffic["source"] if traffic else None,
         "hbm": {"achieved": rb["hbm_gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": rb["hbm_frac"], "peak_source": peaks["source"]},
-        "model": "max(algorithmic bytes / HBM, 16 ex2 per element / MUFU at 148 SM x 16/clk x sm_max_mhz)",
+        "model": f"max(algorithmic bytes / HBM, {nst} ex2 per element / MUFU at 148 SM x 16/clk x sm_max_mhz)",
         "per_op_ms": {"fwd": fwd_ms, "bwd": bwd_ms},
         "fwd_frac": rf["frac"], "step_frac": rs["frac"],
     }
@@ -822,7 +851,7 @@ def main():
         "higher_is_better": True, "scaling": res.get("scaling", "weak"), "vs_baseline": None,
         "dtype": res["dtype"], "data": "synthetic (seeded, BASELINE distributions, generated on device)",
         "config": {"workload": cfg["workload"], "B": cfg["B"], "L": cfg["L"], "D": cfg["D"],
-                   "N": NSTATE, "io_dtype": res["io_dtype"],
+                   "N": cfg.get("nstate", NSTATE), "groups": cfg.get("groups", 1), "io_dtype": res["io_dtype"],
                    "l2": res.get("l2", "inputs + outputs per step (~250 MB at config 3) exceed the "
                                        "126 MB L2; no flush"),
                    "parallelism": res.get("parallelism", f"replicas x{world}: one independent "
