@@ -456,7 +456,9 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
         // (each copy of the recompute loop below is branch-free)
         auto recompute = [&](auto clamp_tag) {
             constexpr bool CLAMP = decltype(clamp_tag)::value;
-#pragma unroll 1
+            // two 4-step blocks per iteration: the second block's loads and exponentials
+            // overlap the first block's serial updates (168 registers, no spills)
+#pragma unroll 2
         for (int i0 = 0; i0 < PB_LT; i0 += 4) {
             float dt[4][2], uu[4][2];
             float4 B4[4];
