@@ -7,7 +7,9 @@
  * plain device pointers, int64 sizes, a dtype code and a cudaStream_t passed as void*.
  * Nothing is allocated inside the library: outputs and workspaces come from the caller
  * (the Python layer allocates them with the PyTorch caching allocator). Calls are
- * reentrant; the only global state is the per-thread error message.
+ * reentrant. Process-wide state: the per-thread error message and last-launch error word,
+ * per-device caches (SM count, the kernels' shared-memory attribute), and the file-scope
+ * device array of mwc_ss_fwd_noalloc (the only state shared between calls on the GPU).
  *
  * All tensors are contiguous row-major with these shapes (N = 16 states):
  *   u, delta, out, du, ddelta, dout : (B, L, D)
@@ -83,6 +85,17 @@ MWC_API int mwc_ss_fwd(const void* u, const void* delta, const void* A, const vo
 
 /* Workspace bytes mwc_ss_bwd needs for (B, L, D) on the current device. */
 MWC_API int64_t mwc_ss_bwd_workspace_bytes(int64_t B, int64_t L, int64_t D, int dtype);
+
+/*
+ * mwc_ss_plan -- the launch plan mwc_ss_fwd (backward = 0) or mwc_ss_bwd (backward = 1) picks
+ * for (B, L, D, dtype) on the current device, assuming 16-byte-aligned buffers. Writes
+ * info[0] = path (MWC_PATH_*), info[1] = K (time segments per 128-channel chain),
+ * info[2] = segment length in time tiles (32 steps forward, 16 backward; the segmented
+ * generic path: steps), info[3] = CTAs of the main launch. For tests and tuning; no
+ * counterpart in the reference (its kernels had one fixed launch shape).
+ */
+enum mwc_path { MWC_PATH_GENERIC = 0, MWC_PATH_CHAINED = 1, MWC_PATH_SPLIT = 2 };
+MWC_API int mwc_ss_plan(int64_t B, int64_t L, int64_t D, int dtype, int backward, int32_t* info);
 
 /*
  * Backward of mwc_ss_fwd for loss = sum(out * dout) + sum(h_last * dh_last): a reverse scan

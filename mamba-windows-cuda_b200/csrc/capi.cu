@@ -428,6 +428,43 @@ int mwc_ss_bwd_grouped(const void* u, const void* delta, const void* A, const vo
                        dD, dh_prev, workspace, workspace_bytes, B, L, D, G, dtype, stream);
 }
 
+int mwc_ss_plan(int64_t B, int64_t L, int64_t D, int dtype, int backward, int32_t* info) {
+    int rc;
+    if (info == nullptr) return fail(MWC_ERR_INVALID, "info (4 x int32) is required");
+    if ((rc = check_dtype(dtype)) != MWC_OK) return rc;
+    if ((rc = check_sizes(B, L, D)) != MWC_OK) return rc;
+    info[0] = MWC_PATH_GENERIC;
+    info[1] = info[2] = info[3] = 0;
+    if (B == 0 || D == 0) return ok();
+    const int sms = device_sms();
+    const bool rows16 = (D * (int64_t)elem_size(dtype)) % 16 == 0 && L <= 0x7fffffffLL && D <= 0x7fffffffLL;
+    PersistPlan pp = backward ? plan_persistent_bwd(B, L, D, sms) : plan_persistent(B, L, D, sms);
+    int path = MWC_PATH_CHAINED;
+    if (!pp.ok) {
+        pp = backward ? plan_persistent_bwd_split(B, L, D, sms) : plan_persistent_split(B, L, D, sms);
+        path = MWC_PATH_SPLIT;
+    }
+    if (pp.ok && rows16) {
+        info[0] = path;
+        info[1] = pp.K;
+        info[2] = pp.seg_tiles;
+        info[3] = pp.grid;
+        return ok();
+    }
+    if (!backward) {
+        const FwdPlan plan = plan_fwd(B, L, D, dtype, sms);
+        info[1] = plan.nseg;
+        info[2] = (int32_t)std::min<int64_t>(plan.seg_len, 0x7fffffff);
+        info[3] = (int32_t)std::min<int64_t>(((D + plan.channels_per_block - 1) / plan.channels_per_block) * B *
+                                                 plan.nseg, 0x7fffffff);
+    } else {
+        info[1] = 1;
+        info[2] = (int32_t)std::min<int64_t>(L, 0x7fffffff);
+        info[3] = (int32_t)std::min<int64_t>(bwd_ws(B, L, D, dtype).nblk * B, 0x7fffffff);
+    }
+    return ok();
+}
+
 int mwc_ss_fixup(const void* delta, const void* A, const void* Cm, const float* h_in,
                  const float* decay, void* out, void* h_last, float* ckpt, int64_t B, int64_t L,
                  int64_t D, int dtype, void* stream) {

@@ -71,11 +71,15 @@ extern "C" MWC_API int mwc_ss_fwd_noalloc(const void* u, const void* delta, cons
                                           const void* h_prev, void* out, void* h_last,
                                           float* ckpt, float* decay, int64_t B, int64_t L,
                                           int64_t D, int dtype, void* stream) {
+    // the segmented kernels have no device waits: nothing for mwc_check_last_launch to read
+    // (an earlier persistent call's error word may belong to a workspace already freed)
+    note_err_word(nullptr);
     if (dtype != MWC_F32 && dtype != MWC_F16 && dtype != MWC_BF16)
         return report_error(MWC_ERR_INVALID, "u must be float32/float16/bfloat16");
     if (B < 0 || L < 0 || D < 0) return report_error(MWC_ERR_INVALID, "negative size");
     if (L == 0) return report_error(MWC_ERR_INVALID, "empty sequence (L=0)");
     if (B > 65535) return report_error(MWC_ERR_UNSUPPORTED, "batch exceeds 65535");
+    if ((D + 3) / 4 > 0x7fffffffLL) return report_error(MWC_ERR_UNSUPPORTED, "D too large");
     if (!u || !delta || !A || !Bm || !Cm || !Dv)
         return report_error(MWC_ERR_INVALID, "u, delta, A, B_ssm, C_ssm and D_ssm are required");
     if (!out && !h_last && !ckpt && !decay) return report_error(MWC_ERR_INVALID, "no output requested");

@@ -188,6 +188,9 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
             if (need_hprev) bytes += rows_bytes;
             if (need_hand) {
                 if (p.mode == 0) flag_wait(&p.flags[c * p.K + k - 1], PF_NCW, p.err);
+                // the record was written with generic-proxy stores (made visible by the
+                // acquire above); the bulk copy below reads it through the async proxy
+                fence_proxy_async_global();
                 bytes += PF_HAND * 4;
             }
             mbar_expect_tx(&s.full[st], bytes);

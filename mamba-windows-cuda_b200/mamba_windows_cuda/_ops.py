@@ -105,6 +105,20 @@ def ckpt_count(L: int) -> int:
     return (L + CK - 1) // CK
 
 
+PATHS = {0: "generic", 1: "chained", 2: "split"}
+
+
+def plan(B: int, L: int, D: int, dtype: torch.dtype, backward: bool = False) -> dict:
+    """The launch plan the forward (or backward) picks for (B, L, D) on the current device,
+    for 16-byte-aligned buffers (mwc_ss_plan): path ("chained": persistent kernel with K
+    chained time segments per 128-channel chain; "split": independent segments + fold;
+    "generic": the non-TMA kernels), K, segment length (tiles), CTAs."""
+    lib = _lib.load()
+    info = (ctypes.c_int32 * 4)()
+    _lib.check(lib.mwc_ss_plan(B, L, D, _DTYPES[dtype], int(bool(backward)), info), "plan query")
+    return {"path": PATHS[info[0]], "K": info[1], "seg": info[2], "grid": info[3]}
+
+
 def ss_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=None, *, want_out=True,
                want_h_last=False, want_ckpt=False, want_decay=False):
     """Run the forward scan. Inputs must be contiguous and validated.

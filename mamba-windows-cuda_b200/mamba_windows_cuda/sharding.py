@@ -58,15 +58,43 @@ def fold_carries(decays: torch.Tensor, states: torch.Tensor, upto: int) -> torch
 
 
 def _cuda_local_scan(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev):
+    """Local scan of a rank's range: (out, h_last, decay, end), where ``end`` is the float32
+    end state. With 16-bit I/O, h_last is rounded to the I/O type, so the end state comes
+    from the last float32 checkpoint instead (the state after the range's last step), and
+    the carries travel and fold in float32 as in the single-GPU scan's segment hand-off."""
     from . import _ops
-    out, h_last, _, decay = _ops.ss_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev,
-                                            want_h_last=True, want_decay=True)
-    return out, h_last, decay
+    half = u.dtype != torch.float32
+    out, h_last, ckpt, decay = _ops.ss_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev,
+                                               want_h_last=True, want_ckpt=half, want_decay=True)
+    end = ckpt[:, -1].contiguous() if half else h_last
+    return out, h_last, decay, end
 
 
-def _cuda_fixup(delta, A, C_ssm, h_in, decay, out, h_last):
+def _cuda_fixup(delta, A, C_ssm, h_in, decay, out, h_last, end=None):
+    """Folds h_in into the rank's output in place; h_last = decay * h_in + end, computed in
+    float32 from the float32 end state when one is given (16-bit I/O)."""
     from . import _ops
-    _ops.ss_fixup(delta, A, C_ssm, h_in, decay, out, h_last)
+    if end is not None and h_last.dtype != torch.float32:
+        _ops.ss_fixup(delta, A, C_ssm, h_in, decay, out, None)
+        h_last.copy_((decay * h_in + end).to(h_last.dtype))
+    else:
+        _ops.ss_fixup(delta, A, C_ssm, h_in, decay, out, h_last)
+
+
+def _split_local(res):
+    """(out, h_last, decay, end32) from a local scan's result; stand-ins that return three
+    values give their h_last as the end state."""
+    if len(res) == 4:
+        return res
+    out, h_last, decay = res
+    return out, h_last, decay, None
+
+
+def _fix(fixup, delta, A, C_ssm, h_in, decay, out, h_last, end):
+    if end is not None and fixup is _cuda_fixup:
+        fixup(delta, A, C_ssm, h_in, decay, out, h_last, end)
+    else:
+        fixup(delta, A, C_ssm, h_in, decay, out, h_last)
 
 
 def _all_gather(payload: torch.Tensor, world: int, group) -> torch.Tensor:
@@ -91,9 +119,10 @@ def sequence_sharded_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=None, *, g
     the state after it (after the last range on the last rank; on every rank with
     ``broadcast_h_last``).
 
-    ``local_scan(u, delta, A, B, C, D, h_prev) -> (out, h_last, decay)`` and
+    ``local_scan(u, delta, A, B, C, D, h_prev) -> (out, h_last, decay[, end32])`` and
     ``fixup(delta, A, C, h_in, decay, out, h_last)`` default to the CUDA entry points (the
-    CPU tests pass float64 restatements).
+    CPU tests pass float64 restatements). The carries are exchanged and folded in float32;
+    with 16-bit I/O the CUDA local scan supplies a float32 end state for them.
     """
     import torch.distributed as dist
     world = dist.get_world_size(group)
@@ -101,12 +130,13 @@ def sequence_sharded_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=None, *, g
     local_scan = local_scan or _cuda_local_scan
     fixup = fixup or _cuda_fixup
 
-    out, h_last, decay = local_scan(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev if rank == 0 else None)
-    payload = torch.stack([decay.float(), h_last.float()]).contiguous()
+    out, h_last, decay, end = _split_local(
+        local_scan(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev if rank == 0 else None))
+    payload = torch.stack([decay.float(), (end if end is not None else h_last).float()]).contiguous()
     gathered = _all_gather(payload, world, group)
     if rank > 0:
         h_in = fold_carries(gathered[:, 0], gathered[:, 1], rank).contiguous()
-        fixup(delta, A, C_ssm, h_in, decay, out, h_last)
+        _fix(fixup, delta, A, C_ssm, h_in, decay, out, h_last, end)
     if broadcast_h_last and world > 1:
         src = world - 1 if group is None else dist.get_global_rank(group, world - 1)
         dist.broadcast(h_last, src=src, group=group)
@@ -129,15 +159,16 @@ def emulated_sequence_sharded_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=N
         sl = (slice(None), slice(a, b))
         parts.append((u[sl].contiguous(), delta[sl].contiguous(), B_ssm[sl].contiguous(),
                       C_ssm[sl].contiguous()))
-    locals_ = [local_scan(p[0], p[1], A, p[2], p[3], D_ssm, h_prev if r == 0 else None)
+    locals_ = [_split_local(local_scan(p[0], p[1], A, p[2], p[3], D_ssm, h_prev if r == 0 else None))
                for r, p in enumerate(parts)]
-    payloads = [torch.stack([dc.float(), hl.float()]) for (_, hl, dc) in locals_]
+    payloads = [torch.stack([dc.float(), (e if e is not None else hl).float()])
+                for (_, hl, dc, e) in locals_]
     outs, h_last = [], None
-    for r, ((o, hl, dc), p) in enumerate(zip(locals_, parts)):
+    for r, ((o, hl, dc, e), p) in enumerate(zip(locals_, parts)):
         if r > 0:
             h_in = fold_carries(torch.stack([q[0] for q in payloads]),
                                 torch.stack([q[1] for q in payloads]), r).contiguous()
-            fixup(p[1], A, p[3], h_in, dc, o, hl)
+            _fix(fixup, p[1], A, p[3], h_in, dc, o, hl, e)
         outs.append(o)
         h_last = hl
     return torch.cat(outs, dim=1), h_last

@@ -62,6 +62,24 @@ def test_size_queries(lib):
     assert lib.mwc_ss_fwd_workspace_bytes(1, 256, 128, 0) == 0
 
 
+def test_plan_query(lib):
+    """mwc_ss_plan reports the path the entry points take (148 SMs assumed without a GPU):
+    the benchmark's config 3 and config 2 run chained persistent segments (K > 1), config 4's
+    chunk the few-chain split passes, short few-channel shapes the generic kernels."""
+    from mamba_windows_cuda import _ops
+    f16 = torch.float16
+    p3f, p3b = _ops.plan(4, 2048, 5120, f16), _ops.plan(4, 2048, 5120, f16, backward=True)
+    assert p3f["path"] == "chained" and p3f["K"] > 1 and p3f["K"] * p3f["seg"] * 32 >= 2048
+    assert p3b["path"] == "chained" and p3b["K"] > 1 and p3b["K"] * p3b["seg"] * 16 >= 2048
+    assert _ops.plan(8, 2048, 4096, f16)["K"] > 1
+    assert _ops.plan(1, 65536, 2048, torch.float32)["path"] == "split"
+    assert _ops.plan(2, 256, 5120, f16)["path"] == "generic"
+    # rows of D x 2 bytes that are not a multiple of 16 bytes never take the TMA paths
+    assert _ops.plan(4, 2048, 5121, f16)["path"] == "generic"
+    info = (ctypes.c_int32 * 4)()
+    assert lib.mwc_ss_plan(1, 16, 16, 7, 0, info) == 1
+
+
 def test_c_abi_rejects_bad_arguments_without_touching_the_gpu(lib):
     nul = None
     fake = ctypes.c_void_p(16)  # never dereferenced: validation fails first

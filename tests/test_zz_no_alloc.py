@@ -6,7 +6,8 @@ the library instead of a caller workspace.
 The test calls it through the C ABI (ctypes) twice in a row on different inputs, with a
 shape whose forward is split into L-segments (so the fixed array is actually used), and
 checks each result against the regular workspace entry point mwc_ss_fwd within the fp32
-tolerance of the other tests (normwise 1e-4) and against the float64 oracle. The file name
+tolerance of the other tests (normwise 1e-4) and against the float64 oracle (fp32: normwise
+1e-4; fp16: elementwise atol 2e-2 / rtol 1e-2). The file name
 makes pytest collect it last.
 """
 import ctypes
@@ -14,7 +15,7 @@ import ctypes
 import pytest
 import torch
 
-from _helpers import assert_fp32, make_inputs, np64
+from _helpers import assert_fp16, assert_fp32, make_inputs, np64
 from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -52,10 +53,13 @@ def test_noalloc_forward_matches_workspace_forward(dtype):
         assert_fp32(h_last, ref_h.double().cpu().numpy(), tol=tol, what=f"h_last (call {call})")
         assert_fp32(ckpt, ref_ck.double().cpu().numpy(), tol=1e-4, what=f"ckpt (call {call})")
         assert_fp32(decay, ref_dc.double().cpu().numpy(), tol=1e-4, what=f"decay (call {call})")
+        o64, h64 = O.ss_fwd(*[np64(t) for t in args], np64(x["h_prev"]))
         if dtype == torch.float32:
-            o64, h64 = O.ss_fwd(*[np64(t) for t in args], np64(x["h_prev"]))
             assert_fp32(out, o64, what=f"out vs oracle (call {call})")
             assert_fp32(h_last, h64, what=f"h_last vs oracle (call {call})")
+        else:   # float64 on the same fp16 inputs, elementwise atol 2e-2 / rtol 1e-2
+            assert_fp16(out, o64, f"out vs oracle (call {call})")
+            assert_fp16(h_last, h64, f"h_last vs oracle (call {call})")
 
 
 def test_noalloc_forward_rejects_bad_arguments():
