@@ -30,6 +30,73 @@ def _prep(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=None):
     return c + [h_prev.contiguous() if h_prev is not None else None]
 
 
+class _SelectiveScanOps:
+    """The op module the reference JIT-built (``_get_selective_scan_cuda_module``,
+    mamba_cuda.py:835-872), with its five entry points (declarations at :793-830), backed by
+    libmwc_b200.so. Arguments, return values and RuntimeError validation follow the
+    reference host functions. One difference in kind: the reference's ``h_bank`` (every
+    state, (B, D, L, 16) in the input dtype) is here the float32 checkpoint tensor
+    (B, ceil(L / 16), D, 16), the state after every 16th step, from which
+    ``selective_scan_cuda_backward_direct`` recomputes the rest; pass it through unchanged."""
+
+    @staticmethod
+    def selective_scan_cuda_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev_opt=None):
+        """mamba_cuda.py:176-269: ``out`` (B, L, D), starting from ``h_prev_opt`` (or 0)."""
+        args = _prep(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev_opt)
+        return _ops.ss_forward(*args)[0]
+
+    @staticmethod
+    def selective_scan_cuda_forward_with_state(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev_opt=None):
+        """mamba_cuda.py:271-359: ``[out, h_last]``."""
+        args = _prep(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev_opt)
+        out, h_last, _, _ = _ops.ss_forward(*args, want_h_last=True)
+        return [out, h_last]
+
+    @staticmethod
+    def selective_scan_cuda_backward(u, delta, A, B_ssm, C_ssm, D_ssm, grad_out):
+        """mamba_cuda.py:564-604 (recompute backward, h0 = 0): rebuilds the checkpoints with
+        a forward pass, then runs the reverse scan. Returns ``[du, ddelta, dA, dB, dC, dD]``."""
+        args = _prep(u, delta, A, B_ssm, C_ssm, D_ssm)[:6]
+        _, _, ckpt, _ = _ops.ss_forward(*args, want_out=False, want_ckpt=True)
+        return list(_ops.ss_backward(*args, None, grad_out.contiguous(), None, ckpt)[:6])
+
+    @staticmethod
+    def selective_scan_cuda_forward_store(u, delta, A, B_ssm, C_ssm, D_ssm):
+        """mamba_cuda.py:747-764: ``[out, h_bank]`` with h0 = 0 (h_bank: float32
+        checkpoints, see the class docstring)."""
+        args = _prep(u, delta, A, B_ssm, C_ssm, D_ssm)[:6]
+        out, _, ckpt, _ = _ops.ss_forward(*args, want_ckpt=True)
+        return [out, ckpt]
+
+    @staticmethod
+    def selective_scan_cuda_backward_direct(u, delta, A, B_ssm, C_ssm, D_ssm, grad_out, h_bank):
+        """mamba_cuda.py:766-790: ``[du, ddelta, dA, dB, dC, dD]`` from the states that
+        ``selective_scan_cuda_forward_store`` returned."""
+        args = _prep(u, delta, A, B_ssm, C_ssm, D_ssm)[:6]
+        Bb, L, D = args[0].shape
+        if (not isinstance(h_bank, torch.Tensor) or h_bank.dtype != torch.float32
+                or tuple(h_bank.shape) != (Bb, _ops.ckpt_count(L), D, _ops.NSTATE)):
+            raise RuntimeError("h_bank must be the float32 (B, ceil(L/16), D, 16) states that "
+                               "selective_scan_cuda_forward_store returned")
+        return list(_ops.ss_backward(*args, None, grad_out.contiguous(), None,
+                                     h_bank.contiguous())[:6])
+
+
+_selective_scan_cuda_module = None
+
+
+def _get_selective_scan_cuda_module():
+    """The op module with the reference's five entry points (mamba_cuda.py:835-872). The
+    reference JIT-compiled it here; this build loads the prebuilt sm_100a library instead
+    and raises if it is missing (there is no CPU fallback)."""
+    global _selective_scan_cuda_module
+    if _selective_scan_cuda_module is None:
+        from . import _lib
+        _lib.load()
+        _selective_scan_cuda_module = _SelectiveScanOps()
+    return _selective_scan_cuda_module
+
+
 class SelectiveScanCudaFunction(torch.autograd.Function):
     """Stateful selective scan: ``(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=None) ->
     (out, h_last)``. Gradients flow to all inputs, ``h_prev`` included, through the CUDA
@@ -63,6 +130,10 @@ class SelectiveScanFn(torch.autograd.Function):
     checkpoints, then runs the reverse scan."""
 
     @staticmethod
+    def _get_module():
+        return _get_selective_scan_cuda_module()
+
+    @staticmethod
     def forward(ctx, u, delta, A, B_ssm, C_ssm, D_ssm):
         u, delta, A, B_ssm, C_ssm, D_ssm, _ = _prep(u, delta, A, B_ssm, C_ssm, D_ssm)
         out, _, _, _ = _ops.ss_forward(u, delta, A, B_ssm, C_ssm, D_ssm)
@@ -83,6 +154,10 @@ class SelectiveScanFnV2(torch.autograd.Function):
     """Default training path (reference V2, mamba_cuda.py:1136-1169). The reference's
     forward stored every state (a (B, D, L, 16) bank); here the forward stores one float32
     state per 16 steps and the backward recomputes the rest in registers."""
+
+    @staticmethod
+    def _get_module():
+        return _get_selective_scan_cuda_module()
 
     @staticmethod
     def forward(ctx, u, delta, A, B_ssm, C_ssm, D_ssm):
@@ -111,6 +186,13 @@ class SelectiveScanCuda(torch.nn.Module):
 
     def __init__(self):
         super().__init__()
+        self._module = None
+
+    def _get_module(self):
+        """The op module (mamba_cuda.py:1185-1188): the reference's five host entry points."""
+        if self._module is None:
+            self._module = _get_selective_scan_cuda_module()
+        return self._module
 
     def forward(self, u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=None):
         if h_prev is not None:
