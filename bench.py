@@ -256,11 +256,35 @@ def sum_over_ranks(x, world, dev):
 
 # ----------------------------------------------------------------------------- CPU side
 
+def host_threads():
+    """Host CPUs this process may run on (the thread count both CPU baselines use: torchrun
+    exports OMP_NUM_THREADS=1, so the count is set explicitly, not inherited)."""
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+def cpu_record():
+    """The CPU baseline's host record: CPU model, logical CPUs, CPUs available to us."""
+    model = ""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return {"cpu_model": model, "os_cpu_count": os.cpu_count(), "cpus_available": host_threads()}
+
+
 def oracle_sample(cfg, target_s, seed=0):
-    """Time the float64 CPU restatement of the reference path on an L-slice of the
-    workload sized to ~target_s seconds. Returns (seconds, bytes, sample_desc, threads)."""
+    """Time the float64 CPU restatement of the reference path (oracle/, OpenMP over channels,
+    all host CPUs) on an L-slice of the workload sized to ~target_s seconds. Returns
+    (seconds, bytes, sample_desc, threads)."""
     from oracle import oracle as O
-    import numpy as np
+    O.set_threads(host_threads())
     B, D = cfg["B"], cfg["D"]
     es = torch.tensor([], dtype=cfg["dtype"]).element_size()
 
@@ -299,20 +323,91 @@ def oracle_sample(cfg, target_s, seed=0):
     return secs, nbytes, desc, O.num_threads()
 
 
+def torch_ref_sample(cfg, target_s, seed=0):
+    """Time the reference's own PyTorch CPU path on an L-slice of the workload: the package's
+    restatement of ``selective_scan_ref`` (the reference's mamba_cuda.py:875-946 with the time
+    axis of its einsum fixed) run forward and then backward through torch autograd, in float32
+    with torch.set_num_threads(all host CPUs); ``parallel_scan_ref`` (pscan.py:153-171) for the
+    linear-recurrence workload. Returns (seconds, bytes, sample_desc, threads) with bytes by the
+    workload's byte model, so the GB/s compares with the other arms."""
+    from mamba_windows_cuda.mamba_cuda import selective_scan_ref
+    from mamba_windows_cuda.pscan import parallel_scan_ref
+    nthr = host_threads()
+    torch.set_num_threads(nthr)
+    B, D = cfg["B"], cfg["D"]
+    es = torch.tensor([], dtype=cfg["dtype"]).element_size()
+
+    def run(Ls):
+        if cfg["mode"] == "pscan":
+            g = torch.Generator().manual_seed(seed)
+            a = torch.rand(B, D, Ls, 1, generator=g) * 0.1 + 0.9
+            x = torch.randn(B, D, Ls, 1, generator=g)
+            t0 = time.perf_counter()
+            parallel_scan_ref(a, x)
+            return time.perf_counter() - t0
+        (u, delta, A, Bm, Cm, Dv), gy = make_ss_inputs(cfg, "cpu", seed, L=Ls)
+        leaves = [t.float().requires_grad_(cfg["mode"] == "fwdbwd") for t in (u, delta, A, Bm, Cm, Dv)]
+        t0 = time.perf_counter()
+        out, _ = selective_scan_ref(*leaves)
+        if cfg["mode"] == "fwdbwd":
+            out.backward(gy.float())
+        return time.perf_counter() - t0
+
+    run(8)   # first call: thread pool and allocator warm-up
+    # autograd over the Python time loop grows faster than linearly in L: double the slice
+    # while it takes under ~40% of the target, and keep the last measurement
+    Ls = 16
+    secs = run(Ls)
+    while secs < 0.4 * target_s and 2 * Ls <= cfg["L"]:
+        Ls *= 2
+        secs = run(Ls)
+    if cfg["mode"] == "pscan":
+        nbytes = 12 * B * D * Ls
+        desc = f"B={B} D={D} L={Ls} (of {cfg['L']}) slice, parallel_scan_ref float32 on CPU"
+    else:
+        nbytes = ss_bytes(B, Ls, D, es, cfg["mode"])
+        desc = (f"B={B} L={Ls} (of {cfg['L']}) D={D} slice, selective_scan_ref float32 fwd"
+                f"{' + autograd bwd' if cfg['mode'] == 'fwdbwd' else ''} on CPU")
+    return secs, nbytes, desc, nthr
+
+
+def cpu_baseline_record(cfg, port_s, torch_s, seed=0):
+    """The cpu_baseline object: the oracle port timed on all host CPUs (the reported value),
+    with the reference's PyTorch CPU path timed beside it as the anchor and the CPU record."""
+    secs, nbytes, desc, threads = oracle_sample(cfg, port_s, seed=seed)
+    rec = {"value": nbytes / secs / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+           "sample": desc, **cpu_record(), "torch_threads": torch.get_num_threads()}
+    if cfg["mode"] in ("fwdbwd", "fwd", "pscan"):
+        ts, tb, tdesc, tthr = torch_ref_sample(cfg, torch_s, seed=seed)
+        rec["torch_reference"] = {"value": tb / ts / 1e9, "unit": "GB/s", "threads": tthr,
+                                  "sample": tdesc}
+        rec["port_over_torch_reference"] = rec["value"] / rec["torch_reference"]["value"]
+        rec["torch_threads"] = torch.get_num_threads()
+    return rec
+
+
 def reference_arm(args, cfg):
-    """Times the reference algorithm (CPU restatement in oracle/) on host cores."""
+    """Times the reference algorithm on the host's CPUs: the float64 C port in oracle/ (the
+    reference's CPU algorithm, OpenMP over channels) with every available CPU, each step a
+    bounded L-slice of the workload; the reference's PyTorch CPU path is timed once beside it."""
     from oracle import oracle as O
     O.build()
     per_step = max(0.2, 90.0 / max(1, args.steps + args.warmup))
-    secs, nbytes, desc, threads = oracle_sample(cfg, per_step)
     times = []
     for i in range(args.warmup + args.steps):
-        s2, b2, _, _ = oracle_sample(cfg, per_step, seed=i)
+        s2, b2, desc, threads = oracle_sample(cfg, per_step, seed=i)
         if i >= args.warmup:
             times.append((s2, b2))
     tot_s = sum(t for t, _ in times)
     tot_b = sum(b for _, b in times)
     gbs = tot_b / tot_s / 1e9
+    base = {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port", "sample": desc,
+            **cpu_record(), "torch_threads": torch.get_num_threads()}
+    if cfg["mode"] in ("fwdbwd", "fwd", "pscan"):
+        ts, tb, tdesc, tthr = torch_ref_sample(cfg, 10.0)
+        base["torch_reference"] = {"value": tb / ts / 1e9, "unit": "GB/s", "threads": tthr,
+                                   "sample": tdesc}
+        base["port_over_torch_reference"] = gbs / base["torch_reference"]["value"]
     line = {
         "impl": "reference", "metric": cfg.get("metric", METRIC), "value": gbs, "unit": "GB/s",
         "n_gpus": args.gpus,
@@ -322,8 +417,7 @@ def reference_arm(args, cfg):
         "data": "synthetic (seeded, BASELINE distributions)",
         "config": {"workload": cfg["workload"], "B": cfg["B"], "L": cfg["L"], "D": cfg["D"],
                    "N": NSTATE, "sample_per_step": desc},
-        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": desc},
+        "cpu_baseline": base,
         "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     emit(line)
@@ -544,6 +638,135 @@ def bench_stream(args, cfg, dev, world, rank, peaks):
                 if world > 1 else "single GPU, 16 chunks chained through h_prev / h_last",
                 l2=f"{3 * B * Lr * D * es / 1e9:.1f} GB of u / delta / y per rank per step, "
                    "far above the 126 MB L2; no flush")
+
+
+def measure_sharded(args, dev, world, rank):
+    """The north star's multi-GPU workloads, measured beside the headline at every N (strong
+    scaling: the total work is fixed, so ms per step should fall as 1/N).
+
+    * config 4, sequence-sharded: the 2^20-token fp32 streaming forward (B=1, D=2048) split
+      along L, rank r owning chunks split_range(16, N, r); per step every rank runs
+      sharding.sequence_sharded_forward (local scan from zero, NCCL all-gather of the float32
+      (decay, end state) pairs, carry fold, mwc_ss_fixup). Reported: ms per step (max over
+      ranks, CUDA events), GB/s of the whole sequence, the per-phase times (max over ranks)
+      and the speed-up against the single-GPU run of the same sequence as 16 chained
+      forward_with_state calls (the reference's streaming use), timed on rank 0.
+    * config 2, batch split: the B=8 inference forward_with_state with batch rows
+      split_range(8, N, r) on rank r; no exchange.
+    """
+    import mamba_windows_cuda as mwc
+    from mamba_windows_cuda import sharding as S
+    steps, warm = max(3, min(args.steps, 10)), 3
+    stream = torch.cuda.current_stream(dev)
+    mod = mwc.SelectiveScanCuda()
+    out = {}
+
+    # ---- config 4: sequence sharding
+    cfg = CONFIGS["c4"]
+    B, Lc, D, nch = cfg["B"], cfg["L"], cfg["D"], cfg["chunks"]
+    es = torch.tensor([], dtype=cfg["dtype"]).element_size()
+    nbytes = ss_bytes(B, Lc * nch, D, es, "stream")
+
+    def chained(u, delta, A, Bm, Cm, Dv):
+        h = torch.zeros(B, D, NSTATE, dtype=cfg["dtype"], device=dev)
+        with torch.no_grad():
+            for c in range(nch):
+                sl = slice(c * Lc, (c + 1) * Lc)
+                _, h = mod.forward_with_state(u[:, sl], delta[:, sl], A, Bm[:, sl], Cm[:, sl], Dv, h)
+        return h
+
+    def time_fn(fn):
+        for _ in range(warm):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / steps
+
+    t1 = None
+    if world == 1 or rank == 0:   # the single-GPU chained run of the whole sequence
+        ins, _ = make_ss_inputs(cfg, dev, seed=3000, L=Lc * nch)
+        t1 = time_fn(lambda: chained(*ins))
+        del ins
+        torch.cuda.empty_cache()
+    barrier_sync(world, dev)
+    rec = {"workload": "config 4: 2^20-token fp32 streaming forward (B=1, D=2048), sequence-sharded "
+                       "along L across the ranks",
+           "ranks": world, "scaling": "strong", "unit": "GB/s"}
+    if world == 1:
+        rec.update(ms_per_step=t1, value=nbytes / (t1 / 1e3) / 1e9, one_gpu_chained_ms=t1,
+                   speedup_vs_one_gpu_chained=1.0,
+                   note="one GPU: the 16 chunks chained through h_prev / h_last")
+    else:
+        c0, c1 = S.split_range(nch, world, rank)
+        ins, _ = make_ss_inputs(cfg, dev, seed=3000 + rank, L=(c1 - c0) * Lc)
+        h0 = torch.zeros(B, D, NSTATE, dtype=cfg["dtype"], device=dev) if rank == 0 else None
+        names = ("local", "gather", "fold", "fixup")
+        evs = [{k: torch.cuda.Event(enable_timing=True) for k in ("start",) + names}
+               for _ in range(steps)]
+
+        def sharded(ev=None):
+            hook = None
+            if ev is not None:
+                ev["start"].record(stream)
+                hook = lambda name: ev[name].record(stream)   # noqa: E731
+            with torch.no_grad():
+                S.sequence_sharded_forward(*ins, h0, phase_hook=hook)
+
+        for _ in range(warm):
+            sharded()
+        barrier_sync(world, dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(steps):
+            sharded(evs[i])
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier_sync(world, dev)
+        ms = max_over_ranks(e0.elapsed_time(e1) / steps, world, dev)
+        prev = ("start",) + names
+        ph = [statistics.mean(e[prev[j]].elapsed_time(e[prev[j + 1]]) for e in evs) for j in range(4)]
+        import torch.distributed as dist
+        pt = torch.tensor(ph, dtype=torch.float64, device=dev)
+        dist.all_reduce(pt, op=dist.ReduceOp.MAX)
+        t1 = max_over_ranks(t1 if t1 is not None else 0.0, world, dev)
+        rec.update(ms_per_step=ms, value=nbytes / (ms / 1e3) / 1e9, one_gpu_chained_ms=t1,
+                   speedup_vs_one_gpu_chained=t1 / ms,
+                   phases_ms_max_over_ranks=dict(zip(names, [float(v) for v in pt.tolist()])),
+                   note="phases: local scan of the rank's chunks (+ fp32 carry record), NCCL "
+                        "all-gather of (decay, end state), carry fold (one linear-scan launch), "
+                        "mwc_ss_fixup; the all-gather includes waiting for the slowest rank")
+        del ins
+        torch.cuda.empty_cache()
+    out["c4_sequence_sharded"] = rec
+
+    # ---- config 2: batch rows split across the ranks
+    cfg = CONFIGS["c2"]
+    Bt, L, D = cfg["B"], cfg["L"], cfg["D"]
+    es = torch.tensor([], dtype=cfg["dtype"]).element_size()
+    b0, b1 = S.split_range(Bt, world, rank)
+    ms = 0.0
+    if b1 > b0:
+        ins, _ = make_ss_inputs(cfg, dev, seed=4000 + rank, B=b1 - b0)
+
+        def fwd():
+            with torch.no_grad():
+                return mod.forward_with_state(*ins)
+
+        ms = time_fn(fwd)
+        del ins
+    barrier_sync(world, dev)
+    ms = max_over_ranks(ms, world, dev)
+    out["c2_batch_split"] = {
+        "workload": "config 2: B=8 L=2048 D=4096 fp16 inference forward_with_state, batch rows "
+                    "split across the ranks (no exchange)",
+        "ranks": world, "rows_per_rank": f"{Bt // world}-{-(-Bt // world)}", "scaling": "strong",
+        "ms_per_step": ms, "value": ss_bytes(Bt, L, D, es, "fwd") / (ms / 1e3) / 1e9, "unit": "GB/s"}
+    return out
 
 
 _JSON_FD = None
@@ -815,6 +1038,8 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c3")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="skip the sequence-sharded config-4 and batch-split config-2 measurements")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     cfg = CONFIGS[args.config]
@@ -859,10 +1084,10 @@ def main():
         "roofline": res["roofline"], "e2e": res["e2e"], "gpu_launches": res["gpu_launches"],
         "clocks": res["clocks"],
     }
+    if args.config == "c3" and not args.no_sharded:
+        line["sharded"] = measure_sharded(args, dev, world, rank)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        secs, nbytes, desc, threads = oracle_sample(cfg, 10.0)
-        line["cpu_baseline"] = {"value": nbytes / secs / 1e9, "unit": "GB/s", "cores": threads,
-                                "kind": "port", "sample": desc}
+        line["cpu_baseline"] = cpu_baseline_record(cfg, 10.0, 8.0)
     if rank == 0:
         emit(line)
     if world > 1:

@@ -50,7 +50,19 @@ def shard(x: torch.Tensor, dim: int, world: int, rank: int) -> torch.Tensor:
 
 def fold_carries(decays: torch.Tensor, states: torch.Tensor, upto: int) -> torch.Tensor:
     """State entering segment ``upto`` of a sequence cut into segments that were each scanned
-    from zero: ``h = 0; for j < upto: h = decays[j] * h + states[j]`` (float32)."""
+    from zero: ``h = 0; for j < upto: h = decays[j] * h + states[j]`` (float32).
+
+    On CUDA tensors this is one launch of the linear-recurrence scan behind
+    ``parallel_scan_fn`` (x_t = a_t x_{t-1} + b_t along the segment axis), the same combine
+    the single-GPU few-chain split uses; elsewhere a loop over the segments."""
+    if upto <= 0:
+        return torch.zeros_like(states[0], dtype=torch.float32)
+    if decays.is_cuda:
+        from . import _ops
+        n = states[0].numel()
+        a = decays[:upto].float().reshape(1, 1, upto, n).contiguous()
+        x = states[:upto].float().reshape(1, 1, upto, n).contiguous()
+        return _ops.lin_scan_forward(a, x)[0, 0, upto - 1].reshape(states[0].shape)
     h = torch.zeros_like(states[0], dtype=torch.float32)
     for j in range(upto):
         h = decays[j].float() * h + states[j].float()
@@ -110,7 +122,8 @@ def _all_gather(payload: torch.Tensor, world: int, group) -> torch.Tensor:
 def sequence_sharded_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=None, *, group=None,
                              broadcast_h_last: bool = False,
                              local_scan: Optional[Callable] = None,
-                             fixup: Optional[Callable] = None):
+                             fixup: Optional[Callable] = None,
+                             phase_hook: Optional[Callable[[str], None]] = None):
     """Forward scan of a sequence split along L across the ranks of ``group``.
 
     Every rank passes its own contiguous time range of ``u, delta, B_ssm, C_ssm`` ((B, L_r, D)
@@ -123,6 +136,8 @@ def sequence_sharded_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=None, *, g
     ``fixup(delta, A, C, h_in, decay, out, h_last)`` default to the CUDA entry points (the
     CPU tests pass float64 restatements). The carries are exchanged and folded in float32;
     with 16-bit I/O the CUDA local scan supplies a float32 end state for them.
+    ``phase_hook(name)``, when given, is called after each phase ("local", "gather", "fold",
+    "fixup") so a caller can record timing events between them.
     """
     import torch.distributed as dist
     world = dist.get_world_size(group)
@@ -130,13 +145,20 @@ def sequence_sharded_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=None, *, g
     local_scan = local_scan or _cuda_local_scan
     fixup = fixup or _cuda_fixup
 
+    hook = phase_hook or (lambda name: None)
     out, h_last, decay, end = _split_local(
         local_scan(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev if rank == 0 else None))
     payload = torch.stack([decay.float(), (end if end is not None else h_last).float()]).contiguous()
+    hook("local")
     gathered = _all_gather(payload, world, group)
+    hook("gather")
     if rank > 0:
         h_in = fold_carries(gathered[:, 0], gathered[:, 1], rank).contiguous()
+        hook("fold")
         _fix(fixup, delta, A, C_ssm, h_in, decay, out, h_last, end)
+    else:
+        hook("fold")
+    hook("fixup")
     if broadcast_h_last and world > 1:
         src = world - 1 if group is None else dist.get_global_rank(group, world - 1)
         dist.broadcast(h_last, src=src, group=group)
