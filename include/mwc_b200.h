@@ -128,6 +128,26 @@ MWC_API int mwc_ss_fixup(const void* delta, const void* A, const void* Cm, const
                  int64_t B, int64_t L, int64_t D, int dtype, void* stream);
 
 /*
+ * Sequence sharding along L (no counterpart in the reference, which runs on one GPU): a rank
+ * scans its time range from a zero state with mwc_ss_fwd_seq, which is mwc_ss_fwd plus
+ * dprefix, float32 (B, mwc_ss_dprefix_count(L), D, 2): per 32-step tile and channel, the
+ * delta prefix sum before the tile and the minimum over the tile's steps of the prefix sum
+ * through each step (decay must be requested too). It is produced on the persistent path
+ * (see mwc_ss_plan); other shapes return MWC_ERR_UNSUPPORTED, and the caller uses
+ * mwc_ss_fixup. mwc_ss_fixup_chunked then applies the incoming state h_in like mwc_ss_fixup,
+ * cut into 256-step chunks that run in parallel, each started from its prefix and skipped
+ * exactly when the incoming state stays below 2^-40 throughout it.
+ */
+MWC_API int64_t mwc_ss_dprefix_count(int64_t L);
+MWC_API int mwc_ss_fwd_seq(const void* u, const void* delta, const void* A, const void* Bm, const void* Cm,
+               const void* Dv, const void* h_prev, void* out, void* h_last, float* ckpt, float* decay,
+               float* dprefix, void* workspace, int64_t workspace_bytes,
+               int64_t B, int64_t L, int64_t D, int dtype, void* stream);
+MWC_API int mwc_ss_fixup_chunked(const void* delta, const void* A, const void* Cm, const float* h_in,
+               const float* decay, const float* dprefix, void* out, void* h_last, float* ckpt,
+               int64_t B, int64_t L, int64_t D, int dtype, void* stream);
+
+/*
  * mwc_ss_fwd_grouped / mwc_ss_bwd_grouped -- mwc_ss_fwd / mwc_ss_bwd with B_ssm and C_ssm (and
  * dB, dC) of shape (B, L, G, 16): channel d reads group d / (D / G). No counterpart in the
  * reference, whose B / C are (B, L, 16) (G = 1, where these equal mwc_ss_fwd / mwc_ss_bwd);

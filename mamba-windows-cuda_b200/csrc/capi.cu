@@ -155,7 +155,7 @@ static int fail_groups_path() {
 static int ss_fwd_impl(const void* u, const void* delta, const void* A, const void* Bm, const void* Cm,
                        const void* Dv, const void* h_prev, void* out, void* h_last, float* ckpt,
                        float* decay, void* workspace, int64_t workspace_bytes, int64_t B, int64_t L,
-                       int64_t D, int64_t G, int dtype, void* stream) {
+                       int64_t D, int64_t G, int dtype, void* stream, float* dpre = nullptr) {
     g_last_err_word = nullptr;
     int rc;
     if ((rc = check_dtype(dtype)) != MWC_OK) return rc;
@@ -165,6 +165,7 @@ static int ss_fwd_impl(const void* u, const void* delta, const void* A, const vo
         return fail(MWC_ERR_INVALID, "u, delta, A, B_ssm, C_ssm and D_ssm are required");
     if (!out && !h_last && !ckpt && !decay)
         return fail(MWC_ERR_INVALID, "no output requested");
+    if (dpre && !decay) return fail(MWC_ERR_INVALID, "dprefix needs the decay output");
     if (B == 0 || D == 0) return ok();
     const int sms = device_sms();
     const size_t es0 = elem_size(dtype);
@@ -193,7 +194,7 @@ static int ss_fwd_impl(const void* u, const void* delta, const void* A, const vo
         if (maps) {
             pa.G = (int)G; pa.cpg = (int)(D / G);
             pa.A = A; pa.Dv = Dv; pa.h_prev = h_prev; pa.h_last = h_last;
-            pa.ckpt = ckpt; pa.decay = decay;
+            pa.ckpt = ckpt; pa.decay = decay; pa.dpre = dpre;
             pa.B = (int)B; pa.L = (int)L; pa.D = (int)D;
             pa.nck = (int)mwc_ss_ckpt_count(L);
             pa.has_out = out != nullptr;
@@ -206,6 +207,10 @@ static int ss_fwd_impl(const void* u, const void* delta, const void* A, const vo
         }
     }
     if (G > 1) return fail_groups_path();
+    if (dpre)
+        return fail(MWC_ERR_UNSUPPORTED,
+                    "dprefix is produced on the persistent path only (16-byte-aligned buffers, rows of "
+                    "D x element size a multiple of 16 bytes, and B*D/128 >= SM count or L >= 512)");
     const FwdPlan plan = plan_fwd(B, L, D, dtype, sms);
     const int64_t need = align_up(fwd_carry_floats(plan, B, D) * 4, 256);
     if (need > 0 && (!workspace || workspace_bytes < need))
@@ -243,6 +248,16 @@ int mwc_ss_fwd(const void* u, const void* delta, const void* A, const void* Bm, 
     return ss_fwd_impl(u, delta, A, Bm, Cm, Dv, h_prev, out, h_last, ckpt, decay, workspace,
                        workspace_bytes, B, L, D, 1, dtype, stream);
 }
+
+int mwc_ss_fwd_seq(const void* u, const void* delta, const void* A, const void* Bm, const void* Cm,
+                   const void* Dv, const void* h_prev, void* out, void* h_last, float* ckpt, float* decay,
+                   float* dprefix, void* workspace, int64_t workspace_bytes, int64_t B, int64_t L,
+                   int64_t D, int dtype, void* stream) {
+    return ss_fwd_impl(u, delta, A, Bm, Cm, Dv, h_prev, out, h_last, ckpt, decay, workspace,
+                       workspace_bytes, B, L, D, 1, dtype, stream, dprefix);
+}
+
+int64_t mwc_ss_dprefix_count(int64_t L) { return L <= 0 ? 0 : (L + DPRE_LT - 1) / DPRE_LT; }
 
 int mwc_ss_fwd_grouped(const void* u, const void* delta, const void* A, const void* Bm,
                        const void* Cm, const void* Dv, const void* h_prev, void* out, void* h_last,
@@ -487,6 +502,35 @@ int mwc_ss_fixup(const void* delta, const void* A, const void* Cm, const float* 
     f.vec = ((D * (int64_t)es) % 16 == 0) && aligned16(delta) && (!out || aligned16(out));
     cudaError_t e = launch_fixup(f, plan, dtype, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "selective-scan fixup launch");
+    return ok();
+}
+
+int mwc_ss_fixup_chunked(const void* delta, const void* A, const void* Cm, const float* h_in,
+                         const float* decay, const float* dprefix, void* out, void* h_last, float* ckpt,
+                         int64_t B, int64_t L, int64_t D, int dtype, void* stream) {
+    int rc;
+    if ((rc = check_dtype(dtype)) != MWC_OK) return rc;
+    if ((rc = check_sizes(B, L, D)) != MWC_OK) return rc;
+    if (!delta || !A || !h_in || !dprefix)
+        return fail(MWC_ERR_INVALID, "delta, A, h_in and dprefix are required");
+    if (out && !Cm) return fail(MWC_ERR_INVALID, "C_ssm is required to correct the output");
+    if (h_last && !decay) return fail(MWC_ERR_INVALID, "decay is required to correct h_last");
+    if (B == 0 || D == 0) return ok();
+    const int64_t chunk = (int64_t)FX_CHUNK_TILES * DPRE_LT;
+    const int64_t nchunk = (L + chunk - 1) / chunk;
+    if (nchunk > 65535) return fail(MWC_ERR_UNSUPPORTED, "sequence too long for the chunked fixup");
+    FwdPlan plan = plan_fwd(B, L, D, dtype, device_sms());
+    plan.nseg = (int)nchunk;
+    plan.seg_len = chunk;
+    const size_t es = elem_size(dtype);
+    FixupArgs f{};
+    f.delta = delta; f.A = A; f.Cm = Cm; f.h_in = h_in; f.decay = decay; f.dpre = dprefix;
+    f.out = out; f.h_last = h_last; f.ckpt = ckpt;
+    f.B = B; f.L = L; f.D = D; f.seg_len = chunk; f.nseg = (int)nchunk;
+    f.nck = (int)mwc_ss_ckpt_count(L); f.mode = 2;
+    f.vec = ((D * (int64_t)es) % 16 == 0) && aligned16(delta) && (!out || aligned16(out));
+    cudaError_t e = launch_fixup(f, plan, dtype, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "selective-scan chunked fixup launch");
     return ok();
 }
 

@@ -9,6 +9,8 @@ namespace mwc {
 
 constexpr int NSTATE = 16;   // N: states per channel (the reference supports only 16)
 constexpr int CK = 16;       // checkpoint / backward recompute chunk, in time steps
+constexpr int DPRE_LT = 32;  // time steps per delta-prefix record (the persistent forward's tile)
+constexpr int FX_CHUNK_TILES = 8;   // records per chunk of the chunked sequence-sharding fixup
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float LN2 = 0.6931471805599453f;
 // safe_exp in the reference clamps the natural exponent to [-88, 88]; in base 2 the

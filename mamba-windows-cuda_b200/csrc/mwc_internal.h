@@ -33,14 +33,17 @@ struct FwdArgs {
 };
 
 // Carry fold + truncated fixup. mode 0: h_in for segment s = 1 + blockIdx.z is folded from
-// `carry`; mode 1: one segment over all of L with the explicit h_in / decay.
+// `carry`; mode 1: one segment over all of L with the explicit h_in / decay; mode 2: as mode 1,
+// with L cut into chunks of FX_CHUNK_TILES 32-step tiles (blockIdx.z), each started from its
+// delta prefix (dpre) and skipped when the incoming state has decayed below 2^-40 throughout.
 struct FixupArgs {
     const void* delta;
     const void* A;
     const void* Cm;
     const float* carry;   // mode 0
-    const float* h_in;    // mode 1
-    const float* decay;   // mode 1 (needed for h_last)
+    const float* h_in;    // modes 1 / 2
+    const float* decay;   // modes 1 / 2 (needed for h_last)
+    const float* dpre;    // mode 2: the forward's per-tile delta prefix records (PFwdArgs::dpre)
     void* out;            // nullable, read-modify-write
     void* h_last;         // nullable
     float* decay_out;     // nullable, mode 0: total decay of the call
@@ -111,6 +114,11 @@ struct PFwdArgs {
     void* h_last;
     float* ckpt;
     float* decay;
+    // nullable (launches with decay, modes 0 / 2): (B, ntiles, D, 2) float32, per 32-step tile
+    // and channel the delta prefix sum before the tile and the minimum over the tile's steps
+    // of the prefix sum through each step; the sequence-sharding fixup uses it to skip the
+    // part of a range where the incoming state has decayed away
+    float* dpre;
     float* hand;     // (chains, K, 128, 17): state + sum(delta) handed to the next segment
     int* flags;      // (chains, K) segment-done flags
     int* counter;    // unit queue head

@@ -170,12 +170,12 @@ __global__ void __launch_bounds__(NW * 32) ss_fixup_kernel(const FixupArgs p) {
     const int64_t d = d0 + cib;
     const bool dv = d < p.D;
     const int64_t b = blockIdx.y;
-    const int seg = (p.mode == 0) ? 1 + (int)blockIdx.z : 0;
+    const int seg = (p.mode == 0) ? 1 + (int)blockIdx.z : (p.mode == 2 ? (int)blockIdx.z : 0);
     const int64_t tbeg = (int64_t)seg * p.seg_len;
     const int64_t tend = min(tbeg + p.seg_len, p.L);
     const int ncols = (int)min((int64_t)CPB, p.D - d0);
     const bool vec = p.vec != 0;
-    const bool last = (p.mode == 1) || (seg == p.nseg - 1);
+    const bool last = (p.mode == 1) || (p.mode == 2 && seg == 0) || (p.mode == 0 && seg == p.nseg - 1);
 
     const T* Ap = static_cast<const T*>(p.A);
     float A2[S], hin[S];
@@ -219,7 +219,7 @@ __global__ void __launch_bounds__(NW * 32) ss_fixup_kernel(const FixupArgs p) {
             const float* hi = p.h_in + (b * p.D + d) * N + sg * S;
 #pragma unroll
             for (int j = 0; j < S; ++j) hin[j] = hi[j];
-            if (p.h_last != nullptr) {
+            if (last && p.h_last != nullptr) {
                 T* hl = static_cast<T*>(p.h_last) + (b * p.D + d) * N + sg * S;
                 const float* dc = p.decay + (b * p.D + d) * N + sg * S;
 #pragma unroll
@@ -234,6 +234,22 @@ __global__ void __launch_bounds__(NW * 32) ss_fixup_kernel(const FixupArgs p) {
     T* yb = p.out ? static_cast<T*>(p.out) + b * p.L * p.D + d0 : nullptr;
     float cum = 0.f;
     bool neg = false;
+    if (p.mode == 2) {
+        // chunk start: the delta prefix before the chunk; the chunk is skipped when every
+        // state of every channel of the CTA stays below 2^-40 of h_in throughout it (the
+        // minimum of the prefix over the chunk's steps bounds the largest factor exactly)
+        const int64_t ntl = (p.L + DPRE_LT - 1) / DPRE_LT;
+        const int64_t k0 = (int64_t)seg * FX_CHUNK_TILES;
+        const int64_t k1 = min(k0 + FX_CHUNK_TILES, ntl);
+        float cmin = INFINITY;
+        if (dv) {
+            const float* r = p.dpre + ((b * ntl + k0) * p.D + d) * 2;
+            cum = r[0];
+            for (int64_t k = k0; k < k1; ++k, r += p.D * 2) cmin = fminf(cmin, r[1]);
+        }
+        const bool skip = !dv || (a2max < 0.f && cmin * a2max < -40.f);
+        if (__syncthreads_and(skip)) return;
+    }
     for (int64_t t0 = tbeg; t0 < tend; t0 += LT) {
         const int nrows = (int)min((int64_t)LT, tend - t0);
         __syncthreads();
@@ -320,7 +336,7 @@ static cudaError_t launch_fwd_t(const FwdArgs& a, const FwdPlan& plan, cudaStrea
 template <typename T, int N, int S>
 static cudaError_t launch_fixup_t(const FixupArgs& a, const FwdPlan& plan, cudaStream_t s) {
     constexpr int CPB = FWD_NW * (32 / (N / S));
-    const unsigned gz = a.mode == 0 ? (unsigned)(plan.nseg - 1) : 1u;
+    const unsigned gz = a.mode == 0 ? (unsigned)(plan.nseg - 1) : a.mode == 2 ? (unsigned)a.nseg : 1u;
     if (gz == 0) return cudaSuccess;
     dim3 grid((unsigned)((a.D + CPB - 1) / CPB), (unsigned)a.B, gz);
     ss_fixup_kernel<T, N, S, FWD_NW><<<grid, FWD_NW * 32, 0, s>>>(a);

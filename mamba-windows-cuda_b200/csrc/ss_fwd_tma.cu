@@ -341,6 +341,13 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
         // negative delta in the tile make the clamp the identity), so each copy of the loop
         // is branch-free.
         const bool want_ck = p.ckpt != nullptr;
+        // delta prefix record of the tile (launches with decay): the prefix before the tile and
+        // the minimum over its steps of the prefix through each step
+        float cstart = 0.f, cmin = 0.f;
+        if constexpr (DECAY) {
+            cstart = sumd;
+            cmin = INFINITY;
+        }
         auto run_tile = [&](auto clamp_tag, auto out_tag) {
             constexpr bool CLAMP = decltype(clamp_tag)::value;
             constexpr bool HAS_OUT = decltype(out_tag)::value;
@@ -353,7 +360,10 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
                     for (int r = 0; r < 8; ++r) {
                         dtv[r] = to_f(s.d[st][i0 + r][ch]);
                         uv[r] = to_f(s.u[st][i0 + r][ch]);
-                        if constexpr (DECAY) sumd += dtv[r];
+                        if constexpr (DECAY) {
+                            sumd += dtv[r];
+                            cmin = fminf(cmin, sumd);
+                        }
                     }
                     fwd_block8<CLAMP>(h2, A2v, dtv, uv, Bf + i0 * NSTATE, Cf + i0 * NSTATE, n0, yv);
                     if constexpr (HAS_OUT) {
@@ -380,6 +390,11 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
         } else {
             if (clamp) run_tile(std::true_type{}, std::false_type{});
             else run_tile(std::false_type{}, std::false_type{});
+        }
+        if constexpr (DECAY) {
+            if (p.dpre != nullptr && half == 0 && dv)
+                *reinterpret_cast<float2*>(p.dpre + (((int64_t)b * p.ntiles + t0 / PF_LT) * p.D + d) * 2) =
+                    make_float2(cstart, cmin);
         }
         // this warp is done with the stage's inputs and with its rows of the y tile
         __syncwarp();
@@ -622,6 +637,7 @@ cudaError_t launch_fwd_persistent_split(PFwdArgs& a, const PersistPlan& pl, int 
     p1.ckpt = nullptr;
     p1.h_last = nullptr;
     p1.decay = nullptr;
+    p1.dpre = nullptr;   // state-only segments sum delta from their own start
     const int grid1 = (int)std::min<int64_t>(pl.grid, (int64_t)pl.nchains * (pl.K - 1));
     e = dtype == 2 ? launch_pf_t<__nv_bfloat16, true>(p1, grid1, s)
       : dtype == 1 ? launch_pf_t<__half, true>(p1, grid1, s)

@@ -39,6 +39,9 @@ SIGNATURES = {
     "mwc_ss_fwd_grouped": (_int, [_vp] * 12 + [_i64] * 5 + [_int, _vp]),
     "mwc_ss_bwd_grouped": (_int, [_vp] * 18 + [_i64] * 5 + [_int, _vp]),
     "mwc_ss_fixup": (_int, [_vp] * 8 + [_i64] * 3 + [_int, _vp]),
+    "mwc_ss_dprefix_count": (_i64, [_i64]),
+    "mwc_ss_fwd_seq": (_int, [_vp] * 13 + [_i64] * 4 + [_int, _vp]),
+    "mwc_ss_fixup_chunked": (_int, [_vp] * 9 + [_i64] * 3 + [_int, _vp]),
     "mwc_lin_scan_fwd": (_int, [_vp] * 3 + [_i64] * 3 + [_int, _vp]),
     "mwc_lin_scan_bwd": (_int, [_vp] * 5 + [_i64] * 3 + [_int, _vp]),
     "mwc_ss_fwd_noalloc": (_int, [_vp] * 11 + [_i64] * 3 + [_int, _vp]),

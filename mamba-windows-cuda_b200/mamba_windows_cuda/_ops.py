@@ -120,10 +120,12 @@ def plan(B: int, L: int, D: int, dtype: torch.dtype, backward: bool = False) -> 
 
 
 def ss_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=None, *, want_out=True,
-               want_h_last=False, want_ckpt=False, want_decay=False):
+               want_h_last=False, want_ckpt=False, want_decay=False, dprefix=None):
     """Run the forward scan. Inputs must be contiguous and validated.
 
-    Returns (out, h_last, ckpt, decay); entries not requested are None.
+    Returns (out, h_last, ckpt, decay); entries not requested are None. ``dprefix``: a float32
+    (B, mwc_ss_dprefix_count(L), D, 2) buffer to receive the delta prefix records of a
+    sequence-sharded local scan (mwc_ss_fwd_seq; needs want_decay and the persistent path).
     """
     Bb, L, D = u.shape
     N = A.shape[1]   # 16 everywhere except the N = 32 / 64 forward (mwc_ss_fwd_nstate)
@@ -152,6 +154,10 @@ def ss_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=None, *, want_out=True,
             rc = lib.mwc_ss_fwd_nstate(_p(u), _p(delta), _p(A), _p(B_ssm), _p(C_ssm), _p(D_ssm),
                                        _p(h_prev), _p(out), _p(h_last), _p(ckpt), _p(decay), _p(ws),
                                        ws_bytes, Bb, L, D, N, dt, _stream(dev))
+        elif dprefix is not None:
+            rc = lib.mwc_ss_fwd_seq(_p(u), _p(delta), _p(A), _p(B_ssm), _p(C_ssm), _p(D_ssm),
+                                    _p(h_prev), _p(out), _p(h_last), _p(ckpt), _p(decay), _p(dprefix),
+                                    _p(ws), ws_bytes, Bb, L, D, dt, _stream(dev))
         elif B_ssm.dim() == 4:   # grouped B / C (B, L, G, 16)
             rc = lib.mwc_ss_fwd_grouped(_p(u), _p(delta), _p(A), _p(B_ssm), _p(C_ssm), _p(D_ssm),
                                         _p(h_prev), _p(out), _p(h_last), _p(ckpt), _p(decay), _p(ws),
@@ -275,8 +281,16 @@ def ss_backward_ex(u, delta, A, B_ssm, C_ssm, D_ssm, z, delta_bias, delta_softpl
     return du, ddelta, dA, dB, dC, dD, dbias, dz, dh_prev
 
 
-def ss_fixup(delta, A, C_ssm, h_in, decay=None, out=None, h_last=None, ckpt=None):
-    """Fold an incoming float32 state h_in (B, D, 16) into a scan run from zero, in place."""
+def dprefix_count(L: int) -> int:
+    """Delta prefix records per channel of a sequence-sharded local scan (one per 32 steps)."""
+    return (L + 31) // 32
+
+
+def ss_fixup(delta, A, C_ssm, h_in, decay=None, out=None, h_last=None, ckpt=None, dprefix=None):
+    """Fold an incoming float32 state h_in (B, D, 16) into a scan run from zero, in place.
+    With the local scan's ``dprefix`` records the time range is processed in parallel chunks
+    that are skipped once h_in has decayed (mwc_ss_fixup_chunked); without them, one pass
+    per channel that stops at the decay horizon (mwc_ss_fixup)."""
     Bb, L, D = delta.shape
     if L == 0 or Bb == 0 or D == 0:
         if h_last is not None and decay is not None:
@@ -286,8 +300,12 @@ def ss_fixup(delta, A, C_ssm, h_in, decay=None, out=None, h_last=None, ckpt=None
     dt = dtype_code(delta)
     dev = delta.device
     with torch.cuda.device(dev):
-        rc = lib.mwc_ss_fixup(_p(delta), _p(A), _p(C_ssm), _p(h_in), _p(decay), _p(out),
-                              _p(h_last), _p(ckpt), Bb, L, D, dt, _stream(dev))
+        if dprefix is not None:
+            rc = lib.mwc_ss_fixup_chunked(_p(delta), _p(A), _p(C_ssm), _p(h_in), _p(decay), _p(dprefix),
+                                          _p(out), _p(h_last), _p(ckpt), Bb, L, D, dt, _stream(dev))
+        else:
+            rc = lib.mwc_ss_fixup(_p(delta), _p(A), _p(C_ssm), _p(h_in), _p(decay), _p(out),
+                                  _p(h_last), _p(ckpt), Bb, L, D, dt, _stream(dev))
     _lib.check(rc, "selective_scan fixup")
 
 

@@ -70,41 +70,51 @@ def fold_carries(decays: torch.Tensor, states: torch.Tensor, upto: int) -> torch
 
 
 def _cuda_local_scan(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev):
-    """Local scan of a rank's range: (out, h_last, decay, end), where ``end`` is the float32
-    end state. With 16-bit I/O, h_last is rounded to the I/O type, so the end state comes
-    from the last float32 checkpoint instead (the state after the range's last step), and
-    the carries travel and fold in float32 as in the single-GPU scan's segment hand-off."""
+    """Local scan of a rank's range: (out, h_last, decay, end, dprefix). ``end`` is the
+    float32 end state: with 16-bit I/O, h_last is rounded to the I/O type, so the end state
+    comes from the last float32 checkpoint instead (the state after the range's last step),
+    and the carries travel and fold in float32 as in the single-GPU scan's segment hand-off.
+    ``dprefix`` holds the range's delta prefix records when the persistent kernel runs the
+    scan (None otherwise); the chunked fixup uses them."""
     from . import _ops
     half = u.dtype != torch.float32
+    Bb, L, D = u.shape
+    dpre = None
+    if _ops.plan(Bb, L, D, u.dtype)["path"] != "generic" and all(
+            t.data_ptr() % 16 == 0 for t in (u, delta, A, B_ssm, C_ssm, D_ssm)):
+        dpre = torch.empty((Bb, _ops.dprefix_count(L), D, 2), dtype=torch.float32, device=u.device)
     out, h_last, ckpt, decay = _ops.ss_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev,
-                                               want_h_last=True, want_ckpt=half, want_decay=True)
+                                               want_h_last=True, want_ckpt=half, want_decay=True,
+                                               dprefix=dpre)
     end = ckpt[:, -1].contiguous() if half else h_last
-    return out, h_last, decay, end
+    return out, h_last, decay, end, dpre
 
 
-def _cuda_fixup(delta, A, C_ssm, h_in, decay, out, h_last, end=None):
+def _cuda_fixup(delta, A, C_ssm, h_in, decay, out, h_last, end=None, dpre=None):
     """Folds h_in into the rank's output in place; h_last = decay * h_in + end, computed in
     float32 from the float32 end state when one is given (16-bit I/O)."""
     from . import _ops
     if end is not None and h_last.dtype != torch.float32:
-        _ops.ss_fixup(delta, A, C_ssm, h_in, decay, out, None)
+        _ops.ss_fixup(delta, A, C_ssm, h_in, decay, out, None, dprefix=dpre)
         h_last.copy_((decay * h_in + end).to(h_last.dtype))
     else:
-        _ops.ss_fixup(delta, A, C_ssm, h_in, decay, out, h_last)
+        _ops.ss_fixup(delta, A, C_ssm, h_in, decay, out, h_last, dprefix=dpre)
 
 
 def _split_local(res):
-    """(out, h_last, decay, end32) from a local scan's result; stand-ins that return three
-    values give their h_last as the end state."""
-    if len(res) == 4:
+    """(out, h_last, decay, end32, dprefix) from a local scan's result; stand-ins that return
+    three values give their h_last as the end state and no prefix records."""
+    if len(res) == 5:
         return res
+    if len(res) == 4:
+        return tuple(res) + (None,)
     out, h_last, decay = res
-    return out, h_last, decay, None
+    return out, h_last, decay, None, None
 
 
-def _fix(fixup, delta, A, C_ssm, h_in, decay, out, h_last, end):
-    if end is not None and fixup is _cuda_fixup:
-        fixup(delta, A, C_ssm, h_in, decay, out, h_last, end)
+def _fix(fixup, delta, A, C_ssm, h_in, decay, out, h_last, end, dpre):
+    if fixup is _cuda_fixup:
+        fixup(delta, A, C_ssm, h_in, decay, out, h_last, end, dpre)
     else:
         fixup(delta, A, C_ssm, h_in, decay, out, h_last)
 
@@ -146,7 +156,7 @@ def sequence_sharded_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=None, *, g
     fixup = fixup or _cuda_fixup
 
     hook = phase_hook or (lambda name: None)
-    out, h_last, decay, end = _split_local(
+    out, h_last, decay, end, dpre = _split_local(
         local_scan(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev if rank == 0 else None))
     payload = torch.stack([decay.float(), (end if end is not None else h_last).float()]).contiguous()
     hook("local")
@@ -155,7 +165,7 @@ def sequence_sharded_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=None, *, g
     if rank > 0:
         h_in = fold_carries(gathered[:, 0], gathered[:, 1], rank).contiguous()
         hook("fold")
-        _fix(fixup, delta, A, C_ssm, h_in, decay, out, h_last, end)
+        _fix(fixup, delta, A, C_ssm, h_in, decay, out, h_last, end, dpre)
     else:
         hook("fold")
     hook("fixup")
@@ -184,13 +194,13 @@ def emulated_sequence_sharded_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=N
     locals_ = [_split_local(local_scan(p[0], p[1], A, p[2], p[3], D_ssm, h_prev if r == 0 else None))
                for r, p in enumerate(parts)]
     payloads = [torch.stack([dc.float(), (e if e is not None else hl).float()])
-                for (_, hl, dc, e) in locals_]
+                for (_, hl, dc, e, _) in locals_]
     outs, h_last = [], None
-    for r, ((o, hl, dc, e), p) in enumerate(zip(locals_, parts)):
+    for r, ((o, hl, dc, e, dp), p) in enumerate(zip(locals_, parts)):
         if r > 0:
             h_in = fold_carries(torch.stack([q[0] for q in payloads]),
                                 torch.stack([q[1] for q in payloads]), r).contiguous()
-            _fix(fixup, p[1], A, p[3], h_in, dc, o, hl, e)
+            _fix(fixup, p[1], A, p[3], h_in, dc, o, hl, e, dp)
         outs.append(o)
         h_last = hl
     return torch.cat(outs, dim=1), h_last

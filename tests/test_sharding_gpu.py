@@ -97,3 +97,35 @@ def test_nccl_sequence_sharding_two_ranks():
     assert_fp32(out, o64, what="out")
     for r in range(world):
         assert_fp32(hs[r], h64, what=f"h_last on rank {r}")
+
+
+@pytest.mark.parametrize("neg", [False, True])
+def test_chunked_fixup_matches_serial_fixup(neg):
+    """mwc_ss_fixup_chunked (parallel 256-step chunks started from the local scan's delta
+    prefix records, skipped once h_in has decayed) against mwc_ss_fixup (one pass per channel
+    up to the decay horizon) on the same local scan, including a stretch of negative deltas,
+    where the incoming state grows again after having decayed."""
+    _need_gpu()
+    B, L, D = 1, 8192, 256
+    x = make_inputs(B, L, D, torch.float32, seed=23, dist="c4", with_state=True, device="cuda")
+    x["delta"] *= 4   # decay horizon ~2.2k steps: most chunks are skipped
+    if neg:
+        x["delta"][:, 6000:6040] = -0.25
+    args = [x[k] for k in ("u", "delta", "A", "Bm", "Cm", "Dv")]
+    assert _ops.plan(B, L, D, torch.float32)["path"] != "generic"
+    dpre = torch.empty(B, _ops.dprefix_count(L), D, 2, device="cuda")
+    out, h_last, ckpt, decay = _ops.ss_forward(*args, want_h_last=True, want_ckpt=True, want_decay=True,
+                                               dprefix=dpre)
+    h_in = x["h_prev"].float().contiguous()
+    res = []
+    for dp in (dpre, None):
+        o, h, c = out.clone(), h_last.clone(), ckpt.clone()
+        _ops.ss_fixup(x["delta"], x["A"], x["Cm"], h_in, decay, o, h, c, dprefix=dp)
+        res.append((o, h, c))
+    torch.cuda.synchronize()
+    for a, b, what in zip(res[0], res[1], ("out", "h_last", "ckpt")):
+        assert_fp32(a, b.double().cpu().numpy(), tol=1e-5, what=what)
+    # and against the oracle scan started from h_in
+    o64, h64 = O.ss_fwd(*[np64(t) for t in args], np64(h_in))
+    assert_fp32(res[0][0], o64, what="out vs oracle")
+    assert_fp32(res[0][1], h64, what="h_last vs oracle")
