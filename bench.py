@@ -85,14 +85,16 @@ CONFIGS = {
 
 
 # DRAM bytes (read + write) of one launch of the dominant kernel, from one ncu capture of
-# this bench's own command (profiles/ss_fwd_bwd_persistent_c3_fp16.md).
+# this bench's own command (`--metrics dram__bytes_read.sum,dram__bytes_write.sum` on the
+# kernel named below; the capture and its command are kept with the profile summaries).
 CAPTURED_TRAFFIC = {
     "c3": {"bytes": 419.284992e6 + 204.703744e6,
-           "source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, ss_bwd_persistent_kernel, "
-                     "profiles/ss_fwd_bwd_persistent_c3_fp16.md"},
+           "source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one ss_bwd_persistent_kernel "
+                     "launch of `python bench.py --steps 3 --warmup 3 --no-cpu-baseline`"},
     "conv": {"bytes": 167.935232e6 + 54.496256e6,
-             "source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, conv1d_bwd_tma_kernel (part of "
-                       "dx is still in L2 at kernel end), profiles/conv1d_tma_conv_fp16.md"},
+             "source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one conv1d_bwd_tma_kernel "
+                       "launch of `python bench.py --config conv --steps 3 --warmup 3 --no-cpu-baseline` "
+                       "(part of dx is still in L2 at kernel end)"},
 }
 
 

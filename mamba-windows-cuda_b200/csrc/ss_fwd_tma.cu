@@ -32,7 +32,13 @@ namespace mwc {
 
 constexpr int PF_LT = 32;
 constexpr int PF_CPB = 128;
-constexpr int PF_NCW = 8;                    // compute warps
+#ifndef MWC_FWD_SPT
+#define MWC_FWD_SPT 8   // states per compute thread: 8 (8 compute warps; 4 with 16 warps measured slower)
+#endif
+constexpr int PF_SPT = MWC_FWD_SPT;
+constexpr int PF_NP = PF_SPT / 2;            // float2 state pairs per thread
+constexpr int PF_LPC = NSTATE / PF_SPT;      // lanes per channel
+constexpr int PF_NCW = PF_CPB * PF_LPC / 32; // compute warps
 constexpr int PF_NT = (PF_NCW + 2) * 32;     // + producer warp + helper warp
 constexpr int PF_HAND = PF_CPB * (NSTATE + 1);  // floats of one segment hand-off record
 static_assert(PF_LT % CK == 0, "a forward tile holds whole checkpoint chunks");
@@ -74,27 +80,28 @@ struct __align__(128) PFwdSmem {
 // exponent of the block is provably <= 0 (A <= 0 and delta >= 0), where the clamp is the
 // identity.
 template <bool CLAMP>
-__device__ __forceinline__ void fwd_block8(float2 (&h2)[4], const float2 (&A2v)[4],
+__device__ __forceinline__ void fwd_block8(float2 (&h2)[PF_NP], const float2 (&A2v)[PF_NP],
                                            const float (&dtv)[8], const float (&uv)[8],
                                            const float* Bf, const float* Cf, int n0,
                                            float (&yv)[8]) {
+    constexpr int NQ = PF_NP / 2;   // float4 groups of the lane's states
 #pragma unroll
     for (int r = 0; r < 8; ++r) {
         const float2 dt2 = make_float2(dtv[r], dtv[r]);
         const float du = dtv[r] * uv[r];
         const float2 du2 = make_float2(du, du);
-        float2 a2[4];
+        float2 a2[PF_NP];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < PF_NP; ++j) {
             const float2 x = __fmul2_rn(dt2, A2v[j]);
             a2[j] = CLAMP ? make_float2(ex2(fminf(x.x, ARG2_HI)), ex2(fminf(x.y, ARG2_HI)))
                           : make_float2(ex2(x.x), ex2(x.y));
         }
         const float4* Bq = reinterpret_cast<const float4*>(Bf + r * NSTATE + n0);
         const float4* Cq = reinterpret_cast<const float4*>(Cf + r * NSTATE + n0);
-        float2 yq[2];
+        float2 yq[NQ];
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
+        for (int q = 0; q < NQ; ++q) {
             const float4 bq = Bq[q];
             const float4 cq = Cq[q];
             h2[2 * q] = __ffma2_rn(a2[2 * q], h2[2 * q], __fmul2_rn(du2, make_float2(bq.x, bq.y)));
@@ -103,7 +110,9 @@ __device__ __forceinline__ void fwd_block8(float2 (&h2)[4], const float2 (&A2v)[
             yq[q] = __fmul2_rn(make_float2(cq.x, cq.y), h2[2 * q]);
             yq[q] = __ffma2_rn(make_float2(cq.z, cq.w), h2[2 * q + 1], yq[q]);
         }
-        const float2 y2 = __fadd2_rn(yq[0], yq[1]);
+        float2 y2 = yq[0];
+#pragma unroll
+        for (int q = 1; q < NQ; ++q) y2 = __fadd2_rn(y2, yq[q]);
         yv[r] = y2.x + y2.y;
     }
 }
@@ -276,10 +285,10 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
     }
 
     // ================================ compute warps ================================
-    const int half = lane & 1;
-    const int ch = w * 16 + (lane >> 1);
-    const int n0 = half * 8;
-    float2 A2v[4], h2[4];
+    const int half = lane % PF_LPC;   // the lane's share of the channel's states
+    const int ch = w * (32 / PF_LPC) + lane / PF_LPC;
+    const int n0 = half * PF_SPT;
+    float2 A2v[PF_NP], h2[PF_NP];
     float sumd = 0.f, Dd = 0.f;
     bool a_nonpos = true;
     int64_t d = 0;
@@ -304,7 +313,7 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
             dv = d < p.D;
             bool nonpos = true;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
+            for (int j = 0; j < PF_NP; ++j) {
                 A2v[j].x = dv ? to_f(s.At[st][ch][n0 + 2 * j]) * LOG2E : 0.f;
                 A2v[j].y = dv ? to_f(s.At[st][ch][n0 + 2 * j + 1]) * LOG2E : 0.f;
                 nonpos = nonpos && A2v[j].x <= 0.f && A2v[j].y <= 0.f;
@@ -314,16 +323,16 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
             if (k == 0 || p.mode == 1) {   // state-only segments after the first start from zero
                 sumd = 0.f;
 #pragma unroll
-                for (int j = 0; j < 4; ++j) h2[j] = make_float2(0.f, 0.f);
+                for (int j = 0; j < PF_NP; ++j) h2[j] = make_float2(0.f, 0.f);
                 if (k == 0 && p.h_prev != nullptr && dv) {
 #pragma unroll
-                    for (int j = 0; j < 4; ++j)
+                    for (int j = 0; j < PF_NP; ++j)
                         h2[j] = make_float2(to_f(s.Ht[st][ch][n0 + 2 * j]), to_f(s.Ht[st][ch][n0 + 2 * j + 1]));
                 }
             } else {
                 const float* hs = &s.hin[st][ch * (NSTATE + 1)];
 #pragma unroll
-                for (int j = 0; j < 4; ++j) h2[j] = make_float2(hs[n0 + 2 * j], hs[n0 + 2 * j + 1]);
+                for (int j = 0; j < PF_NP; ++j) h2[j] = make_float2(hs[n0 + 2 * j], hs[n0 + 2 * j + 1]);
                 sumd = hs[NSTATE];
             }
         }
@@ -369,7 +378,9 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
                     if constexpr (HAS_OUT) {
 #pragma unroll
                         for (int r = 0; r < 8; ++r) {
-                            const float y = yv[r] + __shfl_xor_sync(FULL, yv[r], 1);
+                            float y = yv[r];
+#pragma unroll
+                            for (int o = 1; o < PF_LPC; o <<= 1) y += __shfl_xor_sync(FULL, y, o);
                             if (half == 0) s.y[yb][i0 + r][ch] = from_f<T>(fmaf(Dd, uv[r], y));
                         }
                     }
@@ -378,8 +389,9 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
                 if (want_ck && kk < p.nck && dv) {
                     float4* cp = reinterpret_cast<float4*>(
                         p.ckpt + (((int64_t)b * p.nck + kk) * p.D + d) * NSTATE + n0);
-                    cp[0] = make_float4(h2[0].x, h2[0].y, h2[1].x, h2[1].y);
-                    cp[1] = make_float4(h2[2].x, h2[2].y, h2[3].x, h2[3].y);
+#pragma unroll
+                    for (int q = 0; q < PF_NP / 2; ++q)
+                        cp[q] = make_float4(h2[2 * q].x, h2[2 * q].y, h2[2 * q + 1].x, h2[2 * q + 1].y);
                 }
             }
         };
@@ -410,7 +422,7 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
                 if (p.mode != 2) {   // seeded segments find their records already written
                     float* hs = p.hand + (int64_t)(c * p.K + k) * PF_HAND + ch * (NSTATE + 1);
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
+                    for (int j = 0; j < PF_NP; ++j) {
                         hs[n0 + 2 * j] = h2[j].x;
                         hs[n0 + 2 * j + 1] = h2[j].y;
                     }
@@ -425,7 +437,7 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
                 if (p.h_last != nullptr) {
                     T* hl = static_cast<T*>(p.h_last) + ((int64_t)b * p.D + d) * NSTATE + n0;
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
+                    for (int j = 0; j < PF_NP; ++j) {
                         hl[2 * j] = from_f<T>(h2[j].x);
                         hl[2 * j + 1] = from_f<T>(h2[j].y);
                     }
@@ -433,7 +445,7 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
                 if (p.decay != nullptr) {
                     float* dc = p.decay + ((int64_t)b * p.D + d) * NSTATE + n0;
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
+                    for (int j = 0; j < PF_NP; ++j) {
                         dc[2 * j] = ex2(fminf(A2v[j].x * sumd, ARG2_HI));
                         dc[2 * j + 1] = ex2(fminf(A2v[j].y * sumd, ARG2_HI));
                     }

@@ -1,9 +1,9 @@
 """Generate the golden fixtures in this directory from the reference's own Python code.
 
-Run once, in a container that has the reference checkout (default ``/root/reference``;
-override with ``MWC_REFERENCE_ROOT``)::
+Run once, in a container that has the reference checkout, naming it as the argument or in
+``MWC_REFERENCE_ROOT``::
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py REFERENCE_ROOT
 
 It imports the reference package and records inputs and outputs of:
 
@@ -32,7 +32,7 @@ import sys
 import numpy as np
 import torch
 
-REF_ROOT = os.environ.get("MWC_REFERENCE_ROOT", "/root/reference")
+REF_ROOT = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("MWC_REFERENCE_ROOT", "")
 OUT_DIR = os.path.dirname(os.path.abspath(__file__))
 
 
@@ -98,6 +98,8 @@ def save(name, **arrays):
 
 
 def main():
+    if not REF_ROOT or not os.path.isdir(os.path.join(REF_ROOT, "mamba_windows_cuda")):
+        raise SystemExit("usage: make_golden.py REFERENCE_ROOT (or set MWC_REFERENCE_ROOT)")
     sys.path.insert(0, REF_ROOT)
     import mamba_windows_cuda.mamba_cuda as ref
     import mamba_windows_cuda.pscan as ref_pscan
