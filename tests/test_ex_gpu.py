@@ -47,6 +47,16 @@ CASES = [
     (torch.float16, 4, 256, 5120, True, True, True, False),
     (torch.bfloat16, 2, 200, 64, True, True, True, True),
     (torch.float16, 3, 130, 40, True, True, True, True),         # ragged
+    # the persistent kernels under the transforms: config-3 shape (chained segments), bias
+    # without softplus, bfloat16 with h_prev, and the few-chain split passes in float16
+    (torch.float16, 4, 2048, 5120, True, True, True, False),
+    (torch.float16, 4, 256, 5120, False, True, False, False),
+    (torch.bfloat16, 4, 512, 5120, True, True, True, True),
+    (torch.float16, 1, 4096, 256, True, True, True, True),
+    # ragged L on the persistent kernels (chained segments; split passes; bias only)
+    (torch.float16, 4, 2000, 5120, True, True, True, False),
+    (torch.float16, 1, 1000, 256, True, True, True, True),
+    (torch.float16, 1, 1000, 256, False, True, False, True),
 ]
 
 
