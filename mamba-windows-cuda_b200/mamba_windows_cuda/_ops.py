@@ -31,7 +31,8 @@ def dtype_code(t: torch.Tensor) -> int:
 
 
 def _p(t):
-    return None if t is None else ctypes.c_void_p(t.data_ptr())
+    # a plain int: the entry points declare c_void_p arguments, which take ints and None
+    return None if t is None else t.data_ptr()
 
 
 # MWC_CHECK_WAITS=1: after every forward / backward call, wait for the stream and raise if a
@@ -44,8 +45,44 @@ def _check_waits(lib, dev, what):
         _lib.check(lib.mwc_check_last_launch(_stream(dev)), what)
 
 
-def _stream(device) -> ctypes.c_void_p:
-    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+def _index(device) -> int:
+    return device.index if device.index is not None else torch._C._cuda_getDevice()
+
+
+def _stream(device) -> int:
+    """The raw cudaStream_t of the current stream of ``device`` (what
+    torch.cuda.current_stream(device).cuda_stream returns, without building the Stream
+    object: this is on every call's path)."""
+    return torch._C._cuda_getCurrentRawStream(_index(device))
+
+
+_WS_BYTES = {}
+
+
+def _ws_bytes(lib, name, *shape):
+    """Workspace bytes of an entry point for a shape on the current device, queried once:
+    the sizes depend only on the shape and the device's SM count."""
+    key = (name, torch._C._cuda_getDevice()) + shape
+    v = _WS_BYTES.get(key)
+    if v is None:
+        v = _WS_BYTES[key] = int(getattr(lib, name)(*shape))
+    return v
+
+
+class _on_device:
+    """Make ``device`` the current CUDA device for the block (torch.cuda.device's exchange,
+    without its argument normalisation; a no-op exchange when it already is current)."""
+    __slots__ = ("idx", "prev")
+
+    def __init__(self, device):
+        self.idx = _index(device)
+
+    def __enter__(self):
+        self.prev = torch._C._cuda_exchangeDevice(self.idx)
+
+    def __exit__(self, *exc):
+        torch._C._cuda_maybeExchangeDevice(self.prev)
+        return False
 
 
 def check_ss_inputs(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=None):
@@ -144,11 +181,11 @@ def ss_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=None, *, want_out=True,
         return out, h_last, ckpt, decay
     lib = _lib.load()
     dt = dtype_code(u)
-    with torch.cuda.device(dev):
+    with _on_device(dev):
         if N != NSTATE:
-            ws_bytes = int(lib.mwc_ss_fwd_nstate_workspace_bytes(Bb, L, D, N, dt))
+            ws_bytes = _ws_bytes(lib, "mwc_ss_fwd_nstate_workspace_bytes", Bb, L, D, N, dt)
         else:
-            ws_bytes = int(lib.mwc_ss_fwd_workspace_bytes(Bb, L, D, dt))
+            ws_bytes = _ws_bytes(lib, "mwc_ss_fwd_workspace_bytes", Bb, L, D, dt)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes > 0 else None
         if N != NSTATE:
             rc = lib.mwc_ss_fwd_nstate(_p(u), _p(delta), _p(A), _p(B_ssm), _p(C_ssm), _p(D_ssm),
@@ -196,8 +233,8 @@ def ss_backward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev, dout, dh_last, ckpt,
         return du, ddelta, dA, dB, dC, dD, dh_prev
     lib = _lib.load()
     dt = dtype_code(u)
-    with torch.cuda.device(dev):
-        ws_bytes = int(lib.mwc_ss_bwd_workspace_bytes(Bb, L, D, dt))
+    with _on_device(dev):
+        ws_bytes = _ws_bytes(lib, "mwc_ss_bwd_workspace_bytes", Bb, L, D, dt)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
         args = (_p(u), _p(delta), _p(A), _p(B_ssm), _p(C_ssm), _p(D_ssm), _p(h_prev), _p(dout),
                 _p(dh_last), _p(ckpt), _p(du), _p(ddelta), _p(dA), _p(dB), _p(dC), _p(dD),
@@ -229,8 +266,8 @@ def ss_forward_ex(u, delta, A, B_ssm, C_ssm, D_ssm, z=None, delta_bias=None,
         return out, out_z, h_last, ckpt
     lib = _lib.load()
     dt = dtype_code(u)
-    with torch.cuda.device(dev):
-        ws_bytes = int(lib.mwc_ss_fwd_ex_workspace_bytes(Bb, L, D, dt))
+    with _on_device(dev):
+        ws_bytes = _ws_bytes(lib, "mwc_ss_fwd_ex_workspace_bytes", Bb, L, D, dt)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes > 0 else None
         rc = lib.mwc_ss_fwd_ex(_p(u), _p(delta), _p(A), _p(B_ssm), _p(C_ssm), _p(D_ssm), _p(z),
                                _p(delta_bias), int(bool(delta_softplus)), _p(h_prev), _p(out),
@@ -268,8 +305,8 @@ def ss_backward_ex(u, delta, A, B_ssm, C_ssm, D_ssm, z, delta_bias, delta_softpl
         return du, ddelta, dA, dB, dC, dD, dbias, dz, dh_prev
     lib = _lib.load()
     dt = dtype_code(u)
-    with torch.cuda.device(dev):
-        ws_bytes = int(lib.mwc_ss_bwd_ex_workspace_bytes(Bb, L, D, dt))
+    with _on_device(dev):
+        ws_bytes = _ws_bytes(lib, "mwc_ss_bwd_ex_workspace_bytes", Bb, L, D, dt)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
         rc = lib.mwc_ss_bwd_ex(_p(u), _p(delta), _p(A), _p(B_ssm), _p(C_ssm), _p(D_ssm), _p(z),
                                _p(delta_bias), int(bool(delta_softplus)), _p(h_prev), _p(out),
@@ -299,7 +336,7 @@ def ss_fixup(delta, A, C_ssm, h_in, decay=None, out=None, h_last=None, ckpt=None
     lib = _lib.load()
     dt = dtype_code(delta)
     dev = delta.device
-    with torch.cuda.device(dev):
+    with _on_device(dev):
         if dprefix is not None:
             rc = lib.mwc_ss_fixup_chunked(_p(delta), _p(A), _p(C_ssm), _p(h_in), _p(decay), _p(dprefix),
                                           _p(out), _p(h_last), _p(ckpt), Bb, L, D, dt, _stream(dev))
@@ -317,7 +354,7 @@ def lin_scan_forward(a, x):
         return h
     lib = _lib.load()
     dev = x.device
-    with torch.cuda.device(dev):
+    with _on_device(dev):
         rc = lib.mwc_lin_scan_fwd(_p(a), _p(x), _p(h), Bb * Dd, L, N, dtype_code(x),
                                   _stream(dev))
     _lib.check(rc, "parallel_scan forward")
@@ -332,7 +369,7 @@ def lin_scan_backward(a, h, g):
         return ga, gx
     lib = _lib.load()
     dev = g.device
-    with torch.cuda.device(dev):
+    with _on_device(dev):
         rc = lib.mwc_lin_scan_bwd(_p(a), _p(h), _p(g), _p(ga), _p(gx), Bb * Dd, L, N,
                                   dtype_code(g), _stream(dev))
     _lib.check(rc, "parallel_scan backward")

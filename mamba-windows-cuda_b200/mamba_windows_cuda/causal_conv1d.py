@@ -15,7 +15,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from ._ops import _p, _stream, dtype_code
+from ._ops import _on_device, _p, _stream, dtype_code
 
 __all__ = ["CausalConv1dFn", "causal_conv1d_fn", "causal_conv1d_ref", "conv_state"]
 
@@ -53,7 +53,7 @@ class CausalConv1dFn(torch.autograd.Function):
         W = weight.shape[1]
         y = torch.empty_like(x)
         lib = _lib.load()
-        with torch.cuda.device(x.device):
+        with _on_device(x.device):
             rc = lib.mwc_conv1d_fwd(_p(x), _p(weight), _p(bias), _p(x_prev), _ACT[activation], _p(y),
                                     Bb, L, D, W, dtype_code(x), _stream(x.device))
         _lib.check(rc, "causal_conv1d forward")
@@ -72,7 +72,7 @@ class CausalConv1dFn(torch.autograd.Function):
         db = torch.empty_like(bias) if bias is not None else None
         dxp = torch.empty_like(x_prev) if x_prev is not None and ctx.needs_input_grad[4] else None
         lib = _lib.load()
-        with torch.cuda.device(x.device):
+        with _on_device(x.device):
             ws_bytes = int(lib.mwc_conv1d_bwd_workspace_bytes(Bb, L, D, W))
             ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x.device)
             rc = lib.mwc_conv1d_bwd(_p(x), _p(weight), _p(bias), _p(x_prev), ctx.act, _p(dy), _p(dx),
