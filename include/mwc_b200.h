@@ -148,6 +148,20 @@ MWC_API int mwc_ss_fixup_chunked(const void* delta, const void* A, const void* C
                int64_t B, int64_t L, int64_t D, int dtype, void* stream);
 
 /*
+ * mwc_ss_bwd_seq -- mwc_ss_bwd for one rank's range of a sequence-sharded scan, with the
+ * states that cross range boundaries in float32 (B, D, 16): h_in, the state entering the
+ * range (NULL: zero); q_in, the adjoint entering at the range end (NULL: zero); q_out, the
+ * adjoint at the range start (NULL: not written). ckpt holds the range's true states (the
+ * local scan's checkpoints after mwc_ss_fixup[_chunked] folded h_in into them). The rest is
+ * mwc_ss_bwd's contract. No counterpart in the reference (single GPU).
+ */
+MWC_API int mwc_ss_bwd_seq(const void* u, const void* delta, const void* A, const void* Bm, const void* Cm,
+               const void* Dv, const float* h_in, const void* dout, const float* q_in,
+               const float* ckpt, void* du, void* ddelta, void* dA, void* dB, void* dC, void* dD,
+               float* q_out, void* workspace, int64_t workspace_bytes,
+               int64_t B, int64_t L, int64_t D, int dtype, void* stream);
+
+/*
  * mwc_ss_fwd_grouped / mwc_ss_bwd_grouped -- mwc_ss_fwd / mwc_ss_bwd with B_ssm and C_ssm (and
  * dB, dC) of shape (B, L, G, 16): channel d reads group d / (D / G). No counterpart in the
  * reference, whose B / C are (B, L, 16) (G = 1, where these equal mwc_ss_fwd / mwc_ss_bwd);

@@ -337,7 +337,7 @@ static int ss_bwd_impl(const void* u, const void* delta, const void* A, const vo
                        const void* Dv, const void* h_prev, const void* dout, const void* dh_last,
                        const float* ckpt, void* du, void* ddelta, void* dA, void* dB, void* dC, void* dD,
                        void* dh_prev, void* workspace, int64_t workspace_bytes, int64_t B, int64_t L,
-                       int64_t D, int64_t G, int dtype, void* stream) {
+                       int64_t D, int64_t G, int dtype, void* stream, bool carry32 = false) {
     g_last_err_word = nullptr;
     int rc;
     if ((rc = check_dtype(dtype)) != MWC_OK) return rc;
@@ -383,6 +383,7 @@ static int ss_bwd_impl(const void* u, const void* delta, const void* A, const vo
                 pa.du = du; pa.ddelta = ddelta; pa.dh_prev = dh_prev;
                 pa.B = (int)B; pa.L = (int)L; pa.D = (int)D; pa.nck = (int)nck;
                 pa.G = (int)G; pa.cpg = (int)(D / G);
+                pa.carry32 = carry32 ? 1 : 0;
                 cudaStream_t st = static_cast<cudaStream_t>(stream);
                 cudaError_t e = split ? launch_bwd_persistent_split(pa, pb, dtype, workspace, delta, dout, Cm,
                                                                     dA, dB, dC, dD, st)
@@ -406,6 +407,7 @@ static int ss_bwd_impl(const void* u, const void* delta, const void* A, const vo
     a.u = u; a.delta = delta; a.A = A; a.Bm = Bm; a.Cm = Cm; a.Dv = Dv;
     a.h_prev = h_prev; a.dout = dout; a.dh_last = dh_last; a.ckpt = ckpt;
     a.du = du; a.ddelta = ddelta; a.dh_prev = dh_prev;
+    a.carry32 = carry32 ? 1 : 0;
     a.ws_bc = reinterpret_cast<float*>(ws);
     a.ws_a = reinterpret_cast<float*>(ws + w.off_a);
     a.ws_d = reinterpret_cast<float*>(ws + w.off_d);
@@ -431,6 +433,15 @@ int mwc_ss_bwd(const void* u, const void* delta, const void* A, const void* Bm, 
                int64_t D, int dtype, void* stream) {
     return ss_bwd_impl(u, delta, A, Bm, Cm, Dv, h_prev, dout, dh_last, ckpt, du, ddelta, dA, dB, dC,
                        dD, dh_prev, workspace, workspace_bytes, B, L, D, 1, dtype, stream);
+}
+
+int mwc_ss_bwd_seq(const void* u, const void* delta, const void* A, const void* Bm, const void* Cm,
+                   const void* Dv, const float* h_in, const void* dout, const float* q_in,
+                   const float* ckpt, void* du, void* ddelta, void* dA, void* dB, void* dC, void* dD,
+                   float* q_out, void* workspace, int64_t workspace_bytes, int64_t B, int64_t L,
+                   int64_t D, int dtype, void* stream) {
+    return ss_bwd_impl(u, delta, A, Bm, Cm, Dv, h_in, dout, q_in, ckpt, du, ddelta, dA, dB, dC, dD,
+                       q_out, workspace, workspace_bytes, B, L, D, 1, dtype, stream, true);
 }
 
 int mwc_ss_bwd_grouped(const void* u, const void* delta, const void* A, const void* Bm,

@@ -78,6 +78,7 @@ struct BwdArgs {
     int nck;
     int nblk;
     int vec;
+    int carry32;          // h_prev, dh_last, dh_prev are float32 (B, D, 16), not the I/O type
 };
 
 struct BwdFinalArgs {
@@ -177,6 +178,7 @@ struct PBwdArgs {
     // 2: seeded: the records already hold the adjoint state at each segment's end (written
     //    by the adjoint-only pass and its fold), so no segment waits or publishes.
     int mode;
+    int carry32;     // h_prev, dh_last, dh_prev are float32 (B, D, 16), not the I/O type
 };
 
 struct BwdPersistWs {

@@ -82,10 +82,12 @@ __global__ void __launch_bounds__(NW * 32) ss_bwd_kernel(const BwdArgs p) {
         dA[j] = 0.f;
         q[j] = 0.f;
     }
-    if (p.dh_last != nullptr && dv) {
-        const T* g = static_cast<const T*>(p.dh_last) + (b * p.D + d) * NSTATE + sg * S;
+    if (p.dh_last != nullptr && dv) {   // the I/O type, or float32 with carry32
+        const int64_t off = (b * p.D + d) * NSTATE + sg * S;
 #pragma unroll
-        for (int j = 0; j < S; ++j) q[j] = to_f(g[j]);
+        for (int j = 0; j < S; ++j)
+            q[j] = p.carry32 ? static_cast<const float*>(p.dh_last)[off + j]
+                             : to_f(static_cast<const T*>(p.dh_last)[off + j]);
     }
     const float Dd = dv ? to_f(static_cast<const T*>(p.Dv)[d]) : 0.f;
     float dD = 0.f;
@@ -115,9 +117,11 @@ __global__ void __launch_bounds__(NW * 32) ss_bwd_kernel(const BwdArgs p) {
         if (dv) {
             if (k == 0) {
                 if (p.h_prev != nullptr) {
-                    const T* hp = static_cast<const T*>(p.h_prev) + (b * p.D + d) * NSTATE + sg * S;
+                    const int64_t off = (b * p.D + d) * NSTATE + sg * S;
 #pragma unroll
-                    for (int j = 0; j < S; ++j) h0[j] = to_f(hp[j]);
+                    for (int j = 0; j < S; ++j)
+                        h0[j] = p.carry32 ? static_cast<const float*>(p.h_prev)[off + j]
+                                          : to_f(static_cast<const T*>(p.h_prev)[off + j]);
                 }
             } else {
                 const float* c = p.ckpt + ((b * p.nck + k - 1) * p.D + d) * NSTATE + sg * S;
@@ -205,9 +209,12 @@ __global__ void __launch_bounds__(NW * 32) ss_bwd_kernel(const BwdArgs p) {
     for (int j = 0; j < S; ++j) wa[j] = dA[j];
     if (sg == 0) p.ws_d[b * p.D + d] = dD;
     if (p.dh_prev != nullptr) {
-        T* g = static_cast<T*>(p.dh_prev) + (b * p.D + d) * NSTATE + sg * S;
+        const int64_t off = (b * p.D + d) * NSTATE + sg * S;
 #pragma unroll
-        for (int j = 0; j < S; ++j) g[j] = from_f<T>(q[j]);
+        for (int j = 0; j < S; ++j) {
+            if (p.carry32) static_cast<float*>(p.dh_prev)[off + j] = q[j];
+            else static_cast<T*>(p.dh_prev)[off + j] = from_f<T>(q[j]);
+        }
     }
 }
 

@@ -177,6 +177,19 @@ __device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16* p, const fl
 
 __device__ __forceinline__ float2 f2(float x) { return make_float2(x, x); }
 
+// A (B, D, 16) state row: the I/O type, or float32 when the launch carries its states in
+// float32 (the sequence-sharded backward's h_in / q_in / q_out)
+template <typename T>
+__device__ __forceinline__ void load_state4(float (&v)[4], const void* base, int64_t off, bool c32) {
+    if (c32) load4<float>(v, static_cast<const float*>(base) + off);
+    else load4<T>(v, static_cast<const T*>(base) + off);
+}
+template <typename T>
+__device__ __forceinline__ void store_state4(void* base, int64_t off, const float (&v)[4], bool c32) {
+    if (c32) store4<float>(static_cast<float*>(base) + off, v);
+    else store4<T>(static_cast<T*>(base) + off, v);
+}
+
 template <typename T>
 __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __grid_constant__ PBwdArgs p) {
     // Direct cast (no integer round trip): accesses stay in the shared address space.
@@ -415,7 +428,8 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                 for (int cc = 0; cc < 2; ++cc) {
                     float g4[4] = {0.f, 0.f, 0.f, 0.f};
                     if (p.dh_last != nullptr && dvc[cc])
-                        load4<T>(g4, static_cast<const T*>(p.dh_last) + ((int64_t)b * p.D + dbase + cc) * NSTATE + 4 * sg);
+                        load_state4<T>(g4, p.dh_last, ((int64_t)b * p.D + dbase + cc) * NSTATE + 4 * sg,
+                                       p.carry32 != 0);
                     q[cc][0] = make_float2(g4[0], g4[1]);
                     q[cc][1] = make_float2(g4[2], g4[3]);
                 }
@@ -439,7 +453,8 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                     v = *reinterpret_cast<const float4*>(&s.h0[st][c2 + cc][4 * sg]);
                 } else if (p.h_prev != nullptr) {
                     float hp4[4];
-                    load4<T>(hp4, static_cast<const T*>(p.h_prev) + ((int64_t)b * p.D + dbase + cc) * NSTATE + 4 * sg);
+                    load_state4<T>(hp4, p.h_prev, ((int64_t)b * p.D + dbase + cc) * NSTATE + 4 * sg,
+                                   p.carry32 != 0);
                     v = make_float4(hp4[0], hp4[1], hp4[2], hp4[3]);
                 }
             }
@@ -734,7 +749,8 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
                 for (int cc = 0; cc < 2; ++cc)
                     if (dvc[cc]) {
                         const float v4[4] = {q[cc][0].x, q[cc][0].y, q[cc][1].x, q[cc][1].y};
-                        store4<T>(static_cast<T*>(p.dh_prev) + ((int64_t)b * p.D + dbase + cc) * NSTATE + 4 * sg, v4);
+                        store_state4<T>(p.dh_prev, ((int64_t)b * p.D + dbase + cc) * NSTATE + 4 * sg, v4,
+                                        p.carry32 != 0);
                     }
             }
         }
@@ -810,8 +826,8 @@ constexpr int AJ_LT = 32;
 template <typename T>
 __global__ void __launch_bounds__(256) ss_bwd_adjoint_kernel(
     const T* __restrict__ delta, const T* __restrict__ dout, const T* __restrict__ Cm, const T* __restrict__ A,
-    const T* __restrict__ dh_last, float* __restrict__ hand, float* __restrict__ segsum, int L, int D, int nblk,
-    int nchains, int K, int seg_tiles, int G, int cpg) {
+    const void* __restrict__ dh_last, float* __restrict__ hand, float* __restrict__ segsum, int L, int D,
+    int nblk, int nchains, int K, int seg_tiles, int G, int cpg, int carry32) {
     constexpr int VE = 16 / (int)sizeof(T);   // elements per 16-byte vector
     constexpr int VPR = PB_CPB / VE;          // vectors per 128-channel row
     __shared__ __align__(16) T sd[AJ_LT][PB_CPB];
@@ -836,7 +852,10 @@ __global__ void __launch_bounds__(256) ss_bwd_adjoint_kernel(
         for (int e = 0; e < 2; ++e) {
             const int n = n0 + 2 * j + e;
             av[e] = dv ? to_f(A[d * NSTATE + n]) * LOG2E : 0.f;
-            qv[e] = (kp == 0 && dh_last != nullptr && dv) ? to_f(dh_last[((int64_t)b * D + d) * NSTATE + n]) : 0.f;
+            const int64_t off = ((int64_t)b * D + d) * NSTATE + n;
+            qv[e] = (kp == 0 && dh_last != nullptr && dv)
+                        ? (carry32 ? static_cast<const float*>(dh_last)[off] : to_f(static_cast<const T*>(dh_last)[off]))
+                        : 0.f;
             a_nonpos = a_nonpos && av[e] <= 0.f;
         }
         A2[j] = make_float2(av[0], av[1]);
@@ -1069,8 +1088,8 @@ static cudaError_t bwd_split_passes(PBwdArgs& a, const PersistPlan& pl, float* s
     const T* At = static_cast<const T*>(a.A);
     ss_bwd_adjoint_kernel<T><<<(unsigned)(pl.nchains * (pl.K - 1)), 256, 0, s>>>(
         static_cast<const T*>(delta), static_cast<const T*>(dout), static_cast<const T*>(Cm), At,
-        static_cast<const T*>(a.dh_last), a.hand, segsum, a.L, a.D, pl.nblk, pl.nchains, pl.K, pl.seg_tiles,
-        a.G, a.cpg);
+        a.dh_last, a.hand, segsum, a.L, a.D, pl.nblk, pl.nchains, pl.K, pl.seg_tiles, a.G, a.cpg,
+        a.carry32);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     const int64_t nthr = (int64_t)pl.nchains * PB_CPB * NSTATE;

@@ -209,10 +209,11 @@ def ss_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=None, *, want_out=True,
 
 
 def ss_backward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev, dout, dh_last, ckpt,
-                want_dh_prev=False):
+                want_dh_prev=False, carry32=False):
     """Reverse scan. dout (B,L,D) and dh_last (B,D,16) may be None (zero).
 
-    Returns (du, ddelta, dA, dB, dC, dD, dh_prev) in the input dtype.
+    Returns (du, ddelta, dA, dB, dC, dD, dh_prev) in the input dtype. With ``carry32``
+    (mwc_ss_bwd_seq, the sequence-sharded backward) h_prev, dh_last and dh_prev are float32.
     """
     Bb, L, D = u.shape
     dev = u.device
@@ -224,7 +225,8 @@ def ss_backward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev, dout, dh_last, ckpt,
     dB = torch.empty_like(B_ssm)
     dC = torch.empty_like(C_ssm)
     dD = torch.empty_like(D_ssm)
-    dh_prev = torch.empty((Bb, D, NSTATE), dtype=u.dtype, device=dev) if want_dh_prev else None
+    carry_dtype = torch.float32 if carry32 else u.dtype
+    dh_prev = torch.empty((Bb, D, NSTATE), dtype=carry_dtype, device=dev) if want_dh_prev else None
     if L == 0 or Bb == 0 or D == 0:
         for t in (du, ddelta, dA, dB, dC, dD):
             t.zero_()
@@ -241,6 +243,8 @@ def ss_backward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev, dout, dh_last, ckpt,
                 _p(dh_prev), _p(ws), ws_bytes, Bb, L, D)
         if B_ssm.dim() == 4:   # grouped B / C: dB, dC (B, L, G, 16)
             rc = lib.mwc_ss_bwd_grouped(*args, B_ssm.shape[2], dt, _stream(dev))
+        elif carry32:
+            rc = lib.mwc_ss_bwd_seq(*args, dt, _stream(dev))
         else:
             rc = lib.mwc_ss_bwd(*args, dt, _stream(dev))
     _lib.check(rc, "selective_scan backward")

@@ -18,9 +18,14 @@ Two modes.
   the h_last of the whole sequence, so chunked streaming (``h_prev`` -> ``h_last``) keeps its
   meaning across the sharded sequence (``broadcast_h_last`` hands it to every rank).
 
-The reference runs on one GPU and has neither mode; the local scans are the reference's
-forward (``selective_scan_cuda_forward_with_state``, ``mamba_cuda.py:176-359``). Only the
-forward is sequence-sharded; gradients of a sequence-sharded scan are not provided.
+* Sequence-sharded training (``sequence_sharded_scan``): the same forward keeping float32
+  checkpoints of each range, and a backward across the ranks (local reverse scans, one
+  all-gather of the adjoint carries, a reverse fold, and a second reverse scan on every rank
+  but the last; see the section below).
+
+The reference runs on one GPU and has none of these modes; the local scans are the
+reference's forward and backward (``selective_scan_cuda_forward_with_state``,
+``mamba_cuda.py:176-359``; ``selective_scan_cuda_backward_direct``, ``:766-790``).
 """
 from __future__ import annotations
 
@@ -204,3 +209,189 @@ def emulated_sequence_sharded_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=N
         outs.append(o)
         h_last = hl
     return torch.cat(outs, dim=1), h_last
+
+
+# ---------------------------------------------------------------------------
+# Sequence-sharded training: the forward above keeping what the backward needs, and the
+# backward of the sharded scan.
+#
+# The adjoint is linear in (dout, dh_last) for fixed forward states, so its carries fold
+# like the forward's. Each rank runs the reverse scan over its range from its true incoming
+# state with its own dout (and dh_last on the range's h_last) and a zero adjoint at the range
+# end; this gives q0_r, the adjoint at the range start from the range's own terms (and, on
+# the last rank, the final gradients). The adjoint that enters range r at its end from the
+# later ranks is Q_r = q0_{r+1} + P_{r+1} * Q_{r+1} (Q_{last} = 0; P_r is the range's
+# decay, the same factor the forward carries use), one reverse fold of the all-gathered
+# (P_r, q0_r). Every rank but the last then runs its reverse scan again with the adjoint
+# dh_last + Q_r entering at the end, which gives its gradients.
+# ---------------------------------------------------------------------------
+
+def _cuda_train_forward_local(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev):
+    """Local scan of a rank's range for training: output, h_last, the float32 checkpoints the
+    backward recomputes from, the range decay, the float32 end state and (persistent path)
+    the delta prefix records."""
+    from . import _ops
+    Bb, L, D = u.shape
+    dpre = None
+    if L > 0 and _ops.plan(Bb, L, D, u.dtype)["path"] != "generic" and all(
+            t.data_ptr() % 16 == 0 for t in (u, delta, A, B_ssm, C_ssm, D_ssm)):
+        dpre = torch.empty((Bb, _ops.dprefix_count(L), D, 2), dtype=torch.float32, device=u.device)
+    out, h_last, ckpt, decay = _ops.ss_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev,
+                                               want_h_last=True, want_ckpt=True, want_decay=True,
+                                               dprefix=dpre)
+    # the end state travels in float32: with 16-bit I/O from the last checkpoint (the state
+    # after the range's last step); copied, since the fixup updates the checkpoints in place
+    end = ckpt[:, -1].clone() if (u.dtype != torch.float32 and L > 0) else h_last.float().clone()
+    return {"out": out, "h_last": h_last, "ckpt": ckpt, "decay": decay, "end": end, "dpre": dpre}
+
+
+def _cuda_train_fixup(delta, A, C_ssm, h_in, st):
+    """Folds h_in into a training local scan in place: output, checkpoints and h_last."""
+    from . import _ops
+    h_last = st["h_last"]
+    half = h_last.dtype != torch.float32
+    _ops.ss_fixup(delta, A, C_ssm, h_in, st["decay"], st["out"], None if half else h_last, st["ckpt"],
+                  dprefix=st["dpre"])
+    if half:
+        h_last.copy_((st["decay"] * h_in + st["end"]).to(h_last.dtype))
+
+
+def _cuda_train_backward_local(u, delta, A, B_ssm, C_ssm, D_ssm, h_start, ckpt, dout, dh_last):
+    """Reverse scan of a rank's range from its true incoming state ``h_start`` (None: zero)
+    and the adjoint ``dh_last`` entering at its end (mwc_ss_bwd_seq: both, and the returned
+    adjoint at the range start, in float32, like the forward's carries): (du, ddelta, dA,
+    dB, dC, dD in the input dtype, dh_prev float32)."""
+    from . import _ops
+    hp = h_start.float().contiguous() if h_start is not None else None
+    dh = dh_last.float().contiguous() if dh_last is not None else None
+    return _ops.ss_backward(u, delta, A, B_ssm, C_ssm, D_ssm, hp, dout, dh, ckpt, want_dh_prev=True,
+                            carry32=True)
+
+
+def _train_fwd_phase2(rank, gathered, delta, A, C_ssm, st, fixup):
+    """After the all-gather of (decay, end) records: this rank's incoming state (None on rank
+    0), folded into its local scan."""
+    if rank == 0:
+        return None
+    h_in = fold_carries(gathered[:, 0], gathered[:, 1], rank).contiguous()
+    fixup(delta, A, C_ssm, h_in, st)
+    return h_in
+
+
+def _train_bwd_phase2(rank, world, gathered, ins, h_start, ckpt, grads, dout, dh_last, local_backward):
+    """After the all-gather of (decay, q0) records: this rank's gradients. The last rank's
+    local reverse scan is already complete. Every other rank scans its range again with the
+    whole adjoint entering at the end, dh_last + Q (float32), rather than adding a separate
+    scan of Q's share: the two shares can be large with opposite signs next to the range end,
+    and rounding each to a 16-bit type before the sum would lose the difference."""
+    if rank >= world - 1:
+        return list(grads)
+    later = torch.flip(gathered[rank + 1:], dims=[0])   # ranks world-1 .. rank+1
+    Q = fold_carries(later[:, 0], later[:, 1], world - 1 - rank)
+    if dh_last is not None:
+        Q = Q + dh_last.float()
+    return list(local_backward(*ins, h_start, ckpt, dout, Q.contiguous()))
+
+
+class _SequenceShardedScanFn(torch.autograd.Function):
+    """(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev) of this rank's range -> (out, h_last),
+    with the backward across the ranks. Collectives, the same on every rank: forward one
+    all-gather; backward one all-gather and one all-reduce (dA, dD)."""
+
+    @staticmethod
+    def forward(ctx, u, delta, A, B_ssm, C_ssm, D_ssm, h_prev, group, hooks):
+        import torch.distributed as dist
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+        local_forward, fixup, local_backward = hooks
+        st = local_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev if rank == 0 else None)
+        payload = torch.stack([st["decay"].float(), st["end"].float()]).contiguous()
+        gathered = _all_gather(payload, world, group)
+        h_in = _train_fwd_phase2(rank, gathered, delta, A, C_ssm, st, fixup)
+        h_start = h_in if rank > 0 else h_prev
+        ctx.group, ctx.world, ctx.rank, ctx.local_backward = group, world, rank, local_backward
+        ctx.h_prev_grad = rank == 0 and h_prev is not None
+        ctx.save_for_backward(u, delta, A, B_ssm, C_ssm, D_ssm, h_start, st["ckpt"], st["decay"])
+        return st["out"], st["h_last"]
+
+    @staticmethod
+    def backward(ctx, dout, dh_last):
+        import torch.distributed as dist
+        u, delta, A, B_ssm, C_ssm, D_ssm, h_start, ckpt, decay = ctx.saved_tensors
+        ins = (u, delta, A, B_ssm, C_ssm, D_ssm)
+        dout = dout.contiguous() if dout is not None else torch.zeros_like(u)
+        dh = dh_last.contiguous() if dh_last is not None else None
+        grads = ctx.local_backward(*ins, h_start, ckpt, dout, dh)
+        payload = torch.stack([decay.float(), grads[6].float()]).contiguous()
+        gathered = _all_gather(payload, ctx.world, ctx.group)
+        du, ddelta, dA, dB, dC, dD, dh_prev = _train_bwd_phase2(
+            ctx.rank, ctx.world, gathered, ins, h_start, ckpt, grads, dout, dh, ctx.local_backward)
+        # A and D are the same on every rank: their gradient is the sum of the ranks' shares
+        pack = torch.cat([dA.float().reshape(-1), dD.float().reshape(-1)])
+        dist.all_reduce(pack, group=ctx.group)
+        dA = pack[:dA.numel()].reshape(dA.shape).to(dA.dtype)
+        dD = pack[dA.numel():].reshape(dD.shape).to(dD.dtype)
+        dh_prev = dh_prev.to(h_start.dtype) if ctx.h_prev_grad else None
+        return (du, ddelta, dA, dB, dC, dD, dh_prev, None, None)
+
+
+def sequence_sharded_scan(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=None, *, group=None,
+                          local_forward: Optional[Callable] = None, fixup: Optional[Callable] = None,
+                          local_backward: Optional[Callable] = None):
+    """Selective scan of a sequence split along L across the ranks of ``group``, with
+    gradients (training on sequences sharded over GPUs).
+
+    Arguments as ``sequence_sharded_forward``: this rank's time range of ``u, delta, B_ssm,
+    C_ssm`` (ranges in rank order, see ``split_range``), the full ``A`` and ``D_ssm``, and
+    ``h_prev`` (used on rank 0). Returns ``(out, h_last)``: this rank's output range and the
+    state after it. ``backward`` gives every rank the gradients of its own ranges (du, ddelta,
+    dB, dC), the whole sequence's dA and dD (summed over the ranks, as for any replicated
+    parameter: average them with a data-parallel wrapper, do not sum them again), and, on
+    rank 0, the gradient of ``h_prev``. The forward keeps float32 checkpoints of its range
+    (like the single-GPU training forward). ``local_forward``, ``fixup`` and
+    ``local_backward`` default to the CUDA entry points; the CPU tests pass float64
+    stand-ins."""
+    hooks = (local_forward or _cuda_train_forward_local, fixup or _cuda_train_fixup,
+             local_backward or _cuda_train_backward_local)
+    return _SequenceShardedScanFn.apply(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev, group, hooks)
+
+
+def emulated_sequence_sharded_training(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev, dout, dh_last=None,
+                                       *, world: int, local_forward: Optional[Callable] = None,
+                                       fixup: Optional[Callable] = None,
+                                       local_backward: Optional[Callable] = None):
+    """Forward and backward of the sequence-sharded scan with ``world`` ranks emulated in one
+    process on one device (the same phases as ``sequence_sharded_scan``; for tests). Takes the
+    whole sequence, ``dout`` for the whole output and ``dh_last`` for the sequence's h_last.
+    Returns ``(out, h_last, grads)`` with grads a dict of du, ddelta, dA, dB, dC, dD, dh_prev."""
+    lf = local_forward or _cuda_train_forward_local
+    fx = fixup or _cuda_train_fixup
+    lb = local_backward or _cuda_train_backward_local
+    L = u.shape[1]
+    ranges = [split_range(L, world, r) for r in range(world)]
+
+    def part(t, a, b):
+        return t[:, a:b].contiguous()
+
+    ins = [(part(u, a, b), part(delta, a, b), A, part(B_ssm, a, b), part(C_ssm, a, b), D_ssm)
+           for a, b in ranges]
+    sts = [lf(*x, h_prev if r == 0 else None) for r, x in enumerate(ins)]
+    gathered = torch.stack([torch.stack([s["decay"].float(), s["end"].float()]) for s in sts])
+    h_starts = []
+    for r, (x, s) in enumerate(zip(ins, sts)):
+        h_in = _train_fwd_phase2(r, gathered, x[1], A, x[4], s, fx)
+        h_starts.append(h_in if r > 0 else h_prev)
+    douts = [part(dout, a, b) for a, b in ranges]
+    dhs = [dh_last if r == world - 1 else None for r in range(world)]
+    locals_ = [lb(*x, h_starts[r], sts[r]["ckpt"], douts[r], dhs[r]) for r, x in enumerate(ins)]
+    gathered_b = torch.stack([torch.stack([s["decay"].float(), g[6].float()]) for s, g in zip(sts, locals_)])
+    fin = [_train_bwd_phase2(r, world, gathered_b, x, h_starts[r], sts[r]["ckpt"], locals_[r], douts[r],
+                             dhs[r], lb)
+           for r, x in enumerate(ins)]
+    grads = {
+        "du": torch.cat([f[0] for f in fin], dim=1), "ddelta": torch.cat([f[1] for f in fin], dim=1),
+        "dA": sum(f[2].float() for f in fin), "dB": torch.cat([f[3] for f in fin], dim=1),
+        "dC": torch.cat([f[4] for f in fin], dim=1), "dD": sum(f[5].float() for f in fin),
+        "dh_prev": fin[0][6] if h_prev is not None else None,
+    }
+    out = torch.cat([s["out"] for s in sts], dim=1)
+    return out, sts[-1]["h_last"], grads

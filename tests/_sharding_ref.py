@@ -35,3 +35,26 @@ def fixup(delta, A, Cm, h_in, decay, out, h_last):
     corr = np.einsum("bldn,bdn,bln->bld", pcum, hi, _np(Cm))
     out += torch.from_numpy(corr).to(out.dtype)
     h_last.copy_(torch.from_numpy(_np(decay) * hi + _np(h_last)).to(h_last.dtype))
+
+
+# ---- stand-ins for the hooks of sequence-sharded training (sharding.sequence_sharded_scan) ----
+
+def train_local_forward(u, delta, A, Bm, Cm, Dv, h_prev):
+    out, h_last, decay = local_scan(u, delta, A, Bm, Cm, Dv, h_prev)
+    return {"out": out, "h_last": h_last, "ckpt": None, "decay": decay, "end": h_last.clone(),
+            "dpre": None}
+
+
+def train_fixup(delta, A, Cm, h_in, st):
+    fixup(delta, A, Cm, h_in, st["decay"], st["out"], st["h_last"])
+
+
+def train_local_backward(u, delta, A, Bm, Cm, Dv, h_start, ckpt, dout, dh_last):
+    """float64 oracle reverse scan of one range from its incoming state (ckpt unused)."""
+    g = O.ss_bwd(_np(u), _np(delta), _np(A), _np(Bm), _np(Cm), _np(Dv), _np(dout), _np(h_start),
+                 _np(dh_last))
+    return tuple(torch.from_numpy(g[k]) for k in ("du", "ddelta", "dA", "dB", "dC", "dD", "dh_prev"))
+
+
+TRAIN_HOOKS = dict(local_forward=train_local_forward, fixup=train_fixup,
+                   local_backward=train_local_backward)

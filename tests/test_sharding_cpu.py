@@ -109,3 +109,75 @@ def test_gloo_two_ranks_match_full_scan(mode):
     else:
         assert_fp32(np.concatenate(outs, axis=0), o64, what="out")
         assert_fp32(np.concatenate(hs, axis=0), h64, what="h_last")
+
+
+# ---- sequence-sharded training: backward across the ranks ----
+
+GRAD_KEYS = ("du", "ddelta", "dA", "dB", "dC", "dD", "dh_prev")
+
+
+def _train_case(seed=7, B=2, L=48, D=6):
+    x = _inputs(seed=seed, B=B, L=L, D=D)
+    g = torch.Generator().manual_seed(seed + 1)
+    dout = torch.randn(B, L, D, generator=g)
+    dh_last = torch.randn(B, D, 16, generator=g)
+    return x, dout, dh_last
+
+
+def _oracle_grads(x, dout, dh_last):
+    args = [np64(x[k]) for k in ("u", "delta", "A", "Bm", "Cm", "Dv")]
+    return O.ss_bwd(*args, np64(dout), np64(x["h_prev"]), np64(dh_last))
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 5])
+def test_emulated_sequence_training_matches_full_backward(world):
+    x, dout, dh_last = _train_case()
+    args = [x[k] for k in ("u", "delta", "A", "Bm", "Cm", "Dv")]
+    out, h_last, grads = S.emulated_sequence_sharded_training(*args, x["h_prev"], dout, dh_last,
+                                                              world=world, **R.TRAIN_HOOKS)
+    o64, h64 = O.ss_fwd(*[np64(t) for t in args], np64(x["h_prev"]))
+    assert_fp32(out, o64, what=f"out (world {world})")
+    assert_fp32(h_last, h64, what=f"h_last (world {world})")
+    ref = _oracle_grads(x, dout, dh_last)
+    for k in GRAD_KEYS:
+        assert_fp32(grads[k], ref[k], what=f"{k} (world {world})")
+
+
+def _gloo_train_worker(rank, world, port, outdir):
+    import torch.distributed as dist
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world)
+    try:
+        x, dout, dh_last = _train_case(seed=13, B=2, L=40, D=6)
+        a, b = S.split_range(x["u"].shape[1], world, rank)
+        leaves = {k: (x[k][:, a:b] if x[k].dim() == 3 else x[k]).clone().requires_grad_(True)
+                  for k in ("u", "delta", "A", "Bm", "Cm", "Dv")}
+        hp = x["h_prev"].clone().requires_grad_(True)
+        out, h_last = S.sequence_sharded_scan(*leaves.values(), hp, **R.TRAIN_HOOKS)
+        loss = (out * dout[:, a:b].to(out.dtype)).sum()
+        if rank == world - 1:
+            loss = loss + (h_last * dh_last.to(h_last.dtype)).sum()
+        loss.backward()
+        for k, t in leaves.items():
+            np.save(os.path.join(outdir, f"{k}{rank}.npy"), t.grad.double().numpy())
+        np.save(os.path.join(outdir, f"hp{rank}.npy"),
+                hp.grad.double().numpy() if hp.grad is not None else np.zeros(0))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_two_ranks_training_matches_full_backward():
+    world = 2
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_gloo_train_worker, args=(world, _free_port(), d), nprocs=world,
+                           start_method="spawn", join=True)
+        got = {k: [np.load(os.path.join(d, f"{k}{r}.npy")) for r in range(world)]
+               for k in ("u", "delta", "A", "Bm", "Cm", "Dv", "hp")}
+    x, dout, dh_last = _train_case(seed=13, B=2, L=40, D=6)
+    ref = _oracle_grads(x, dout, dh_last)
+    for name, k in (("du", "u"), ("ddelta", "delta"), ("dB", "Bm"), ("dC", "Cm")):
+        assert_fp32(np.concatenate(got[k], axis=1), ref[name], what=name)
+    for r in range(world):   # replicated parameters: every rank holds the sum
+        assert_fp32(got["A"][r], ref["dA"], what=f"dA on rank {r}")
+        assert_fp32(got["Dv"][r], ref["dD"], what=f"dD on rank {r}")
+    assert_fp32(got["hp"][0], ref["dh_prev"], what="dh_prev (rank 0)")

@@ -129,3 +129,101 @@ def test_chunked_fixup_matches_serial_fixup(neg):
     o64, h64 = O.ss_fwd(*[np64(t) for t in args], np64(h_in))
     assert_fp32(res[0][0], o64, what="out vs oracle")
     assert_fp32(res[0][1], h64, what="h_last vs oracle")
+
+
+# ---- sequence-sharded training (forward + backward across the ranks) ----
+# Tolerances: float32 normwise 1e-4; 16-bit per-element gradients (du, ddelta, dh_prev)
+# elementwise atol 2e-2 / rtol 1e-2 (bfloat16: rtol 2e-2), the sums (dA, dB, dC, dD) with
+# atol scaled by max(1, max|ref|), as in the single-GPU parity tests.
+
+TRAIN_CASES = [
+    # (dtype, B, L, D, world, dist)
+    (torch.float32, 1, 8192, 256, 4, "c4"),    # few chains: split passes per range; slow decay
+    (torch.float32, 2, 3000, 96, 3, "c1"),     # ragged ranges on the generic kernels
+    (torch.float16, 1, 8192, 256, 2, "c4"),
+    (torch.bfloat16, 1, 4096, 256, 3, "c4"),
+    (torch.float16, 4, 1024, 5120, 2, "c3"),   # chained persistent kernels per range
+]
+PER_ELEMENT = ("du", "ddelta", "dh_prev")
+
+
+def _check_grad(x, ref, dtype, what, reduced):
+    if dtype == torch.float32:
+        assert_fp32(x, ref, what=what)
+        return
+    atol = 2e-2 * (max(1.0, float(np.abs(ref).max())) if reduced else 1.0)
+    rtol = 2e-2 if dtype == torch.bfloat16 else 1e-2
+    assert_fp16(x.float(), ref, what=what, atol=atol, rtol=rtol)
+
+
+@pytest.mark.parametrize("dtype,B,L,D,world,dist", TRAIN_CASES)
+def test_emulated_sequence_training(dtype, B, L, D, world, dist):
+    _need_gpu()
+    x = make_inputs(B, L, D, dtype, seed=23, dist=dist, with_state=True, device="cuda")
+    args = [x[k] for k in ("u", "delta", "A", "Bm", "Cm", "Dv")]
+    g = torch.Generator(device="cuda").manual_seed(77)
+    dout = torch.randn(B, L, D, generator=g, device="cuda").to(dtype)
+    dh_last = torch.randn(B, D, 16, generator=g, device="cuda").to(dtype)
+    out, h_last, grads = S.emulated_sequence_sharded_training(*args, x["h_prev"], dout, dh_last,
+                                                              world=world)
+    torch.cuda.synchronize()
+    n = [np64(t) for t in args]
+    o64, h64 = O.ss_fwd(*n, np64(x["h_prev"]))
+    ref = O.ss_bwd(*n, np64(dout), np64(x["h_prev"]), np64(dh_last))
+    _check_grad(out, o64, dtype, "out", False)
+    _check_grad(h_last, h64, dtype, "h_last", False)
+    for k in ("du", "ddelta", "dA", "dB", "dC", "dD", "dh_prev"):
+        _check_grad(grads[k], ref[k], dtype, k, k not in PER_ELEMENT)
+
+
+def _nccl_train_worker(rank, world, port, outdir):
+    import datetime
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        dev = f"cuda:{rank}"
+        x = make_inputs(1, 16384, 512, torch.float32, seed=33, dist="c4", with_state=True, device=dev)
+        g = torch.Generator(device=dev).manual_seed(79)
+        dout = torch.randn(1, 16384, 512, generator=g, device=dev)
+        dh_last = torch.randn(1, 512, 16, generator=g, device=dev)
+        a, b = S.split_range(16384, world, rank)
+        leaves = [(x[k][:, a:b] if x[k].dim() == 3 else x[k]).clone().requires_grad_(True)
+                  for k in ("u", "delta", "A", "Bm", "Cm", "Dv")]
+        hp = x["h_prev"].clone().requires_grad_(True)
+        out, h_last = S.sequence_sharded_scan(*leaves, hp)
+        loss = (out * dout[:, a:b]).sum()
+        if rank == world - 1:
+            loss = loss + (h_last * dh_last).sum()
+        loss.backward()
+        torch.cuda.synchronize()
+        for k, t in zip(("du", "ddelta", "dA", "dB", "dC", "dD"), leaves):
+            np.save(os.path.join(outdir, f"{k}{rank}.npy"), t.grad.double().cpu().numpy())
+        if rank == 0:
+            np.save(os.path.join(outdir, "dh_prev.npy"), hp.grad.double().cpu().numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_nccl_sequence_training_two_ranks():
+    _need_gpu(2)
+    world = 2
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_nccl_train_worker, args=(world, _free_port(), d), nprocs=world,
+                           start_method="spawn", join=True)
+        got = {k: [np.load(os.path.join(d, f"{k}{r}.npy")) for r in range(world)]
+               for k in ("du", "ddelta", "dA", "dB", "dC", "dD")}
+        dhp = np.load(os.path.join(d, "dh_prev.npy"))
+    x = make_inputs(1, 16384, 512, torch.float32, seed=33, dist="c4", with_state=True, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(79)
+    dout = torch.randn(1, 16384, 512, generator=g, device="cuda")
+    dh_last = torch.randn(1, 512, 16, generator=g, device="cuda")
+    args = [np64(x[k]) for k in ("u", "delta", "A", "Bm", "Cm", "Dv")]
+    ref = O.ss_bwd(*args, np64(dout), np64(x["h_prev"]), np64(dh_last))
+    for k in ("du", "ddelta", "dB", "dC"):
+        assert_fp32(np.concatenate(got[k], axis=1), ref[k], what=k)
+    for r in range(world):
+        assert_fp32(got["dA"][r], ref["dA"], what=f"dA on rank {r}")
+        assert_fp32(got["dD"][r], ref["dD"], what=f"dD on rank {r}")
+    assert_fp32(dhp, ref["dh_prev"], what="dh_prev")
