@@ -129,9 +129,10 @@ def _oracle_grads(x, dout, dh_last):
     return O.ss_bwd(*args, np64(dout), np64(x["h_prev"]), np64(dh_last))
 
 
-@pytest.mark.parametrize("world", [1, 2, 3, 5])
-def test_emulated_sequence_training_matches_full_backward(world):
-    x, dout, dh_last = _train_case()
+@pytest.mark.parametrize("world,L", [(1, 48), (2, 48), (3, 48), (5, 48), (5, 3)])
+def test_emulated_sequence_training_matches_full_backward(world, L):
+    # (5, 3): more ranks than steps, so some ranges are empty
+    x, dout, dh_last = _train_case(L=L)
     args = [x[k] for k in ("u", "delta", "A", "Bm", "Cm", "Dv")]
     out, h_last, grads = S.emulated_sequence_sharded_training(*args, x["h_prev"], dout, dh_last,
                                                               world=world, **R.TRAIN_HOOKS)

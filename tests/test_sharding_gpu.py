@@ -143,6 +143,8 @@ TRAIN_CASES = [
     (torch.float16, 1, 8192, 256, 2, "c4"),
     (torch.bfloat16, 1, 4096, 256, 3, "c4"),
     (torch.float16, 4, 1024, 5120, 2, "c3"),   # chained persistent kernels per range
+    (torch.float32, 2, 13, 64, 8, "c1"),       # ranges of 0-2 steps (empty ranges too)
+    (torch.float16, 2, 1000, 36, 3, "c1"),     # generic kernels (72-byte rows), ranges ending mid-chunk
 ]
 PER_ELEMENT = ("du", "ddelta", "dh_prev")
 
