@@ -148,6 +148,19 @@ MWC_API int mwc_ss_fixup_chunked(const void* delta, const void* A, const void* C
                int64_t B, int64_t L, int64_t D, int dtype, void* stream);
 
 /*
+ * mwc_ss_adjoint_seq -- the adjoint state at the start of a time range, float32 (B, D, 16):
+ * q_L = q_in (NULL: zero), q_t = a_t (dout_t C_t + q_{t+1}), q_out = q_0, with
+ * a_t = exp(min(delta_t A, 88)) per state: what a rank of a sequence-sharded backward hands
+ * to the ranks before it, without the gradients of a full reverse scan (one exp and two
+ * multiply-adds per element and state). Workspace: mwc_ss_adjoint_seq_workspace_bytes(B, L,
+ * D) bytes, 16-byte aligned. No counterpart in the reference (single GPU).
+ */
+MWC_API int64_t mwc_ss_adjoint_seq_workspace_bytes(int64_t B, int64_t L, int64_t D);
+MWC_API int mwc_ss_adjoint_seq(const void* delta, const void* A, const void* Cm, const void* dout,
+               const float* q_in, float* q_out, void* workspace, int64_t workspace_bytes,
+               int64_t B, int64_t L, int64_t D, int dtype, void* stream);
+
+/*
  * mwc_ss_bwd_seq -- mwc_ss_bwd for one rank's range of a sequence-sharded scan, with the
  * states that cross range boundaries in float32 (B, D, 16): h_in, the state entering the
  * range (NULL: zero); q_in, the adjoint entering at the range end (NULL: zero); q_out, the

@@ -516,6 +516,33 @@ int mwc_ss_fixup(const void* delta, const void* A, const void* Cm, const float* 
     return ok();
 }
 
+int64_t mwc_ss_adjoint_seq_workspace_bytes(int64_t B, int64_t L, int64_t D) {
+    if (B <= 0 || L <= 0 || D <= 0) return 0;
+    return 2 * B * adjoint_seq_chunks(L) * D * NSTATE * (int64_t)sizeof(float);
+}
+
+int mwc_ss_adjoint_seq(const void* delta, const void* A, const void* Cm, const void* dout, const float* q_in,
+                       float* q_out, void* workspace, int64_t workspace_bytes, int64_t B, int64_t L,
+                       int64_t D, int dtype, void* stream) {
+    int rc;
+    if ((rc = check_dtype(dtype)) != MWC_OK) return rc;
+    if ((rc = check_sizes(B, L, D)) != MWC_OK) return rc;
+    if (!delta || !A || !Cm || !dout || !q_out)
+        return fail(MWC_ERR_INVALID, "delta, A, C_ssm, dout and q_out are required");
+    if (B == 0 || D == 0) return ok();
+    if (adjoint_seq_chunks(L) > 65535 || B > 65535)
+        return fail(MWC_ERR_UNSUPPORTED, "sequence or batch too long for the range adjoint");
+    const int64_t need = mwc_ss_adjoint_seq_workspace_bytes(B, L, D);
+    if (!workspace || workspace_bytes < need)
+        return fail(MWC_ERR_WORKSPACE, "range-adjoint workspace of %lld bytes required, got %lld",
+                    (long long)need, (long long)workspace_bytes);
+    if (!aligned16(workspace)) return fail(MWC_ERR_WORKSPACE, "range-adjoint workspace must be 16-byte aligned");
+    cudaError_t e = launch_adjoint_seq(delta, A, Cm, dout, q_in, q_out, static_cast<float*>(workspace), B, L, D,
+                                       dtype, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "range-adjoint launch");
+    return ok();
+}
+
 int mwc_ss_fixup_chunked(const void* delta, const void* A, const void* Cm, const float* h_in,
                          const float* decay, const float* dprefix, void* out, void* h_last, float* ckpt,
                          int64_t B, int64_t L, int64_t D, int dtype, void* stream) {

@@ -237,6 +237,11 @@ cudaError_t launch_fixup(const FixupArgs& a, const FwdPlan& plan, int dtype, cud
 cudaError_t launch_bwd(const BwdArgs& a, int dtype, cudaStream_t s);
 cudaError_t launch_bwd_final(const BwdFinalArgs& a, int dtype, cudaStream_t s);
 cudaError_t launch_lin_fwd(const LinArgs& a, int dtype, cudaStream_t s);
+// Adjoint at the start of a time range (ss_adjoint.cu): ws holds 2 x B x chunks x D x 16 floats.
+int64_t adjoint_seq_chunks(int64_t L);
+cudaError_t launch_adjoint_seq(const void* delta, const void* A, const void* Cm, const void* dout,
+                               const float* q_in, float* q_out, float* ws, int64_t B, int64_t L, int64_t D,
+                               int dtype, cudaStream_t s);
 cudaError_t launch_lin_bwd(const LinArgs& a, int dtype, cudaStream_t s);
 
 // One CTA waits on an mbarrier nothing arrives at, with a short bounded limit; records

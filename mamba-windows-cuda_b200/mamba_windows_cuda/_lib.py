@@ -34,6 +34,8 @@ SIGNATURES = {
     "mwc_ss_bwd_workspace_bytes": (_i64, [_i64, _i64, _i64, _int]),
     "mwc_ss_bwd": (_int, [_vp] * 18 + [_i64] * 4 + [_int, _vp]),
     "mwc_ss_bwd_seq": (_int, [_vp] * 18 + [_i64] * 4 + [_int, _vp]),
+    "mwc_ss_adjoint_seq_workspace_bytes": (_i64, [_i64, _i64, _i64]),
+    "mwc_ss_adjoint_seq": (_int, [_vp] * 7 + [_i64] * 4 + [_int, _vp]),
     "mwc_ss_plan": (_int, [_i64] * 3 + [_int, _int, ctypes.POINTER(ctypes.c_int32)]),
     "mwc_ss_fwd_nstate_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64, _int]),
     "mwc_ss_fwd_nstate": (_int, [_vp] * 12 + [_i64] * 5 + [_int, _vp]),

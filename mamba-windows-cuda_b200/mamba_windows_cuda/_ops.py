@@ -252,6 +252,27 @@ def ss_backward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev, dout, dh_last, ckpt,
     return du, ddelta, dA, dB, dC, dD, dh_prev
 
 
+def ss_adjoint(delta, A, C_ssm, dout, q_in=None):
+    """Adjoint state at the start of a time range (mwc_ss_adjoint_seq): float32 (B, D, 16),
+    from the adjoint ``q_in`` (float32, or None for zero) entering at the range end and the
+    range's output gradient ``dout``."""
+    Bb, L, D = delta.shape
+    dev = delta.device
+    q_out = torch.empty((Bb, D, NSTATE), dtype=torch.float32, device=dev)
+    if L == 0 or Bb == 0 or D == 0:
+        q_out.copy_(q_in) if q_in is not None else q_out.zero_()
+        return q_out
+    lib = _lib.load()
+    dt = dtype_code(delta)
+    with _on_device(dev):
+        ws_bytes = _ws_bytes(lib, "mwc_ss_adjoint_seq_workspace_bytes", Bb, L, D)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        rc = lib.mwc_ss_adjoint_seq(_p(delta), _p(A), _p(C_ssm), _p(dout), _p(q_in), _p(q_out), _p(ws),
+                                    ws_bytes, Bb, L, D, dt, _stream(dev))
+    _lib.check(rc, "selective_scan range adjoint")
+    return q_out
+
+
 def ss_forward_ex(u, delta, A, B_ssm, C_ssm, D_ssm, z=None, delta_bias=None,
                   delta_softplus=False, h_prev=None, *, want_h_last=False, want_ckpt=False):
     """Forward scan with the delta transform (bias, softplus) and the z gate

@@ -216,14 +216,15 @@ def emulated_sequence_sharded_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=N
 # backward of the sharded scan.
 #
 # The adjoint is linear in (dout, dh_last) for fixed forward states, so its carries fold
-# like the forward's. Each rank runs the reverse scan over its range from its true incoming
-# state with its own dout (and dh_last on the range's h_last) and a zero adjoint at the range
-# end; this gives q0_r, the adjoint at the range start from the range's own terms (and, on
-# the last rank, the final gradients). The adjoint that enters range r at its end from the
-# later ranks is Q_r = q0_{r+1} + P_{r+1} * Q_{r+1} (Q_{last} = 0; P_r is the range's
-# decay, the same factor the forward carries use), one reverse fold of the all-gathered
-# (P_r, q0_r). Every rank but the last then runs its reverse scan again with the adjoint
-# dh_last + Q_r entering at the end, which gives its gradients.
+# like the forward's. Each rank first finds q0_r, the adjoint at its range start from the
+# range's own terms (its dout, and dh_last on its h_last) with a zero adjoint at the range
+# end: the last rank by its full reverse scan, which already gives its final gradients; the
+# others by the range-adjoint pass (mwc_ss_adjoint_seq), which computes only that adjoint.
+# The adjoint that enters range r at its end from the later ranks is
+# Q_r = q0_{r+1} + P_{r+1} * Q_{r+1} (Q_{last} = 0; P_r is the range's decay, the same
+# factor the forward carries use), one reverse fold of the all-gathered (P_r, q0_r). Every
+# rank but the last then runs its reverse scan with the adjoint dh_last + Q_r entering at the
+# end, which gives its gradients.
 # ---------------------------------------------------------------------------
 
 def _cuda_train_forward_local(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev):
@@ -268,6 +269,15 @@ def _cuda_train_backward_local(u, delta, A, B_ssm, C_ssm, D_ssm, h_start, ckpt, 
                             carry32=True)
 
 
+def _cuda_train_adjoint_local(u, delta, A, B_ssm, C_ssm, D_ssm, dout, dh_last):
+    """Adjoint at the start of a rank's range from its own dout and the adjoint ``dh_last``
+    entering at its end (mwc_ss_adjoint_seq, float32): the first backward pass of the ranks
+    before the last, which only hand this adjoint on."""
+    from . import _ops
+    q_in = dh_last.float().contiguous() if dh_last is not None else None
+    return _ops.ss_adjoint(delta, A, C_ssm, dout, q_in)
+
+
 def _train_fwd_phase2(rank, gathered, delta, A, C_ssm, st, fixup):
     """After the all-gather of (decay, end) records: this rank's incoming state (None on rank
     0), folded into its local scan."""
@@ -276,6 +286,16 @@ def _train_fwd_phase2(rank, gathered, delta, A, C_ssm, st, fixup):
     h_in = fold_carries(gathered[:, 0], gathered[:, 1], rank).contiguous()
     fixup(delta, A, C_ssm, h_in, st)
     return h_in
+
+
+def _train_bwd_phase1(rank, world, ins, h_start, ckpt, dout, dh_last, local_backward, local_adjoint):
+    """Before the all-gather: (gradients or None, q0). The last rank's reverse scan is already
+    final; the others only need q0 here, the adjoint at their range start from their own
+    terms, which the range-adjoint pass gives without a full reverse scan."""
+    if rank == world - 1:
+        grads = local_backward(*ins, h_start, ckpt, dout, dh_last)
+        return grads, grads[6]
+    return None, local_adjoint(*ins, dout, dh_last)
 
 
 def _train_bwd_phase2(rank, world, gathered, ins, h_start, ckpt, grads, dout, dh_last, local_backward):
@@ -302,13 +322,14 @@ class _SequenceShardedScanFn(torch.autograd.Function):
     def forward(ctx, u, delta, A, B_ssm, C_ssm, D_ssm, h_prev, group, hooks):
         import torch.distributed as dist
         world, rank = dist.get_world_size(group), dist.get_rank(group)
-        local_forward, fixup, local_backward = hooks
+        local_forward, fixup, local_backward, local_adjoint = hooks
         st = local_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev if rank == 0 else None)
         payload = torch.stack([st["decay"].float(), st["end"].float()]).contiguous()
         gathered = _all_gather(payload, world, group)
         h_in = _train_fwd_phase2(rank, gathered, delta, A, C_ssm, st, fixup)
         h_start = h_in if rank > 0 else h_prev
-        ctx.group, ctx.world, ctx.rank, ctx.local_backward = group, world, rank, local_backward
+        ctx.group, ctx.world, ctx.rank = group, world, rank
+        ctx.local_backward, ctx.local_adjoint = local_backward, local_adjoint
         ctx.h_prev_grad = rank == 0 and h_prev is not None
         ctx.save_for_backward(u, delta, A, B_ssm, C_ssm, D_ssm, h_start, st["ckpt"], st["decay"])
         return st["out"], st["h_last"]
@@ -320,8 +341,9 @@ class _SequenceShardedScanFn(torch.autograd.Function):
         ins = (u, delta, A, B_ssm, C_ssm, D_ssm)
         dout = dout.contiguous() if dout is not None else torch.zeros_like(u)
         dh = dh_last.contiguous() if dh_last is not None else None
-        grads = ctx.local_backward(*ins, h_start, ckpt, dout, dh)
-        payload = torch.stack([decay.float(), grads[6].float()]).contiguous()
+        grads, q0 = _train_bwd_phase1(ctx.rank, ctx.world, ins, h_start, ckpt, dout, dh,
+                                      ctx.local_backward, ctx.local_adjoint)
+        payload = torch.stack([decay.float(), q0.float()]).contiguous()
         gathered = _all_gather(payload, ctx.world, ctx.group)
         du, ddelta, dA, dB, dC, dD, dh_prev = _train_bwd_phase2(
             ctx.rank, ctx.world, gathered, ins, h_start, ckpt, grads, dout, dh, ctx.local_backward)
@@ -336,7 +358,8 @@ class _SequenceShardedScanFn(torch.autograd.Function):
 
 def sequence_sharded_scan(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=None, *, group=None,
                           local_forward: Optional[Callable] = None, fixup: Optional[Callable] = None,
-                          local_backward: Optional[Callable] = None):
+                          local_backward: Optional[Callable] = None,
+                          local_adjoint: Optional[Callable] = None):
     """Selective scan of a sequence split along L across the ranks of ``group``, with
     gradients (training on sequences sharded over GPUs).
 
@@ -347,18 +370,19 @@ def sequence_sharded_scan(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=None, *, grou
     dB, dC), the whole sequence's dA and dD (summed over the ranks, as for any replicated
     parameter: average them with a data-parallel wrapper, do not sum them again), and, on
     rank 0, the gradient of ``h_prev``. The forward keeps float32 checkpoints of its range
-    (like the single-GPU training forward). ``local_forward``, ``fixup`` and
-    ``local_backward`` default to the CUDA entry points; the CPU tests pass float64
+    (like the single-GPU training forward). ``local_forward``, ``fixup``, ``local_backward``
+    and ``local_adjoint`` default to the CUDA entry points; the CPU tests pass float64
     stand-ins."""
     hooks = (local_forward or _cuda_train_forward_local, fixup or _cuda_train_fixup,
-             local_backward or _cuda_train_backward_local)
+             local_backward or _cuda_train_backward_local, local_adjoint or _cuda_train_adjoint_local)
     return _SequenceShardedScanFn.apply(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev, group, hooks)
 
 
 def emulated_sequence_sharded_training(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev, dout, dh_last=None,
                                        *, world: int, local_forward: Optional[Callable] = None,
                                        fixup: Optional[Callable] = None,
-                                       local_backward: Optional[Callable] = None):
+                                       local_backward: Optional[Callable] = None,
+                                       local_adjoint: Optional[Callable] = None):
     """Forward and backward of the sequence-sharded scan with ``world`` ranks emulated in one
     process on one device (the same phases as ``sequence_sharded_scan``; for tests). Takes the
     whole sequence, ``dout`` for the whole output and ``dh_last`` for the sequence's h_last.
@@ -366,6 +390,7 @@ def emulated_sequence_sharded_training(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev,
     lf = local_forward or _cuda_train_forward_local
     fx = fixup or _cuda_train_fixup
     lb = local_backward or _cuda_train_backward_local
+    la = local_adjoint or _cuda_train_adjoint_local
     L = u.shape[1]
     ranges = [split_range(L, world, r) for r in range(world)]
 
@@ -382,8 +407,10 @@ def emulated_sequence_sharded_training(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev,
         h_starts.append(h_in if r > 0 else h_prev)
     douts = [part(dout, a, b) for a, b in ranges]
     dhs = [dh_last if r == world - 1 else None for r in range(world)]
-    locals_ = [lb(*x, h_starts[r], sts[r]["ckpt"], douts[r], dhs[r]) for r, x in enumerate(ins)]
-    gathered_b = torch.stack([torch.stack([s["decay"].float(), g[6].float()]) for s, g in zip(sts, locals_)])
+    ph1 = [_train_bwd_phase1(r, world, x, h_starts[r], sts[r]["ckpt"], douts[r], dhs[r], lb, la)
+           for r, x in enumerate(ins)]
+    locals_ = [p[0] for p in ph1]
+    gathered_b = torch.stack([torch.stack([s["decay"].float(), p[1].float()]) for s, p in zip(sts, ph1)])
     fin = [_train_bwd_phase2(r, world, gathered_b, x, h_starts[r], sts[r]["ckpt"], locals_[r], douts[r],
                              dhs[r], lb)
            for r, x in enumerate(ins)]

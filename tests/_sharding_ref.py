@@ -58,3 +58,13 @@ def train_local_backward(u, delta, A, Bm, Cm, Dv, h_start, ckpt, dout, dh_last):
 
 TRAIN_HOOKS = dict(local_forward=train_local_forward, fixup=train_fixup,
                    local_backward=train_local_backward)
+
+
+def train_local_adjoint(u, delta, A, Bm, Cm, Dv, dout, dh_last):
+    """Adjoint at the range start from a zero state's reverse scan (the oracle's dh_prev; the
+    adjoint does not depend on the forward states)."""
+    g = O.ss_bwd(_np(u), _np(delta), _np(A), _np(Bm), _np(Cm), _np(Dv), _np(dout), None, _np(dh_last))
+    return torch.from_numpy(g["dh_prev"])
+
+
+TRAIN_HOOKS["local_adjoint"] = train_local_adjoint

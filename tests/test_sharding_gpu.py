@@ -229,3 +229,25 @@ def test_nccl_sequence_training_two_ranks():
         assert_fp32(got["dA"][r], ref["dA"], what=f"dA on rank {r}")
         assert_fp32(got["dD"][r], ref["dD"], what=f"dD on rank {r}")
     assert_fp32(dhp, ref["dh_prev"], what="dh_prev")
+
+
+@pytest.mark.parametrize("dtype,B,L,D,with_q", [
+    (torch.float32, 2, 1000, 96, True),     # ragged last chunk
+    (torch.float32, 1, 100, 40, False),     # one partial chunk
+    (torch.float16, 1, 4096, 256, True),
+    (torch.bfloat16, 2, 777, 64, True),
+])
+def test_range_adjoint_matches_oracle(dtype, B, L, D, with_q):
+    """mwc_ss_adjoint_seq: the adjoint at the range start against the float64 oracle's
+    dh_prev (the adjoint does not depend on the forward states)."""
+    _need_gpu()
+    x = make_inputs(B, L, D, dtype, seed=41, dist="c4", device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(43)
+    dout = torch.randn(B, L, D, generator=g, device="cuda").to(dtype)
+    q_in = torch.randn(B, D, 16, generator=g, device="cuda") if with_q else None
+    q0 = _ops.ss_adjoint(x["delta"], x["A"], x["Cm"], dout, q_in)
+    torch.cuda.synchronize()
+    args = [np64(x[k]) for k in ("u", "delta", "A", "Bm", "Cm", "Dv")]
+    ref = O.ss_bwd(*args, np64(dout), None, np64(q_in) if with_q else None)["dh_prev"]
+    assert q0.dtype == torch.float32
+    assert_fp32(q0, ref, what="range adjoint")
