@@ -746,6 +746,11 @@ def measure_sharded(args, dev, world, rank):
         torch.cuda.empty_cache()
     out["c4_sequence_sharded"] = rec
 
+    # ---- config 4's first TRAIN_CHUNKS chunks trained (forward + backward) across the ranks
+    if world > 1:
+        out["c4_sequence_sharded_training"] = _sharded_training(cfg, dev, world, rank, steps, warm,
+                                                                stream, mod, time_fn)
+
     # ---- config 2: batch rows split across the ranks
     cfg = CONFIGS["c2"]
     Bt, L, D = cfg["B"], cfg["L"], cfg["D"]
@@ -769,6 +774,71 @@ def measure_sharded(args, dev, world, rank):
         "ranks": world, "rows_per_rank": f"{Bt // world}-{-(-Bt // world)}", "scaling": "strong",
         "ms_per_step": ms, "value": ss_bytes(Bt, L, D, es, "fwd") / (ms / 1e3) / 1e9, "unit": "GB/s"}
     return out
+
+
+TRAIN_CHUNKS = 4   # 2^18 tokens: per-rank ranges up to 2^28 elements at D = 2048
+
+
+def _sharded_training(cfg, dev, world, rank, steps, warm, stream, mod, time_fn):
+    """Forward + backward of sharding.sequence_sharded_scan over config 4's first
+    TRAIN_CHUNKS chunks split along L (rank r owns split_range(tokens, N, r)), against the
+    same tokens trained on one GPU (rank 0) as TRAIN_CHUNKS chained 65,536-step calls with
+    h_prev / h_last and autograd through the chain."""
+    from mamba_windows_cuda import sharding as S
+    from mamba_windows_cuda.mamba_cuda import SelectiveScanCudaFunction
+    B, Lc, D = cfg["B"], cfg["L"], cfg["D"]
+    Lt = Lc * TRAIN_CHUNKS
+    a, b = S.split_range(Lt, world, rank)
+    ins, gy = make_ss_inputs(cfg, dev, seed=3100 + rank, L=b - a)
+    leaves = [t.clone().requires_grad_(True) for t in ins]
+
+    def step():
+        for t in leaves:
+            t.grad = None
+        o, _ = S.sequence_sharded_scan(*leaves, None)
+        o.backward(gy)
+
+    for _ in range(warm):
+        step()
+    barrier_sync(world, dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world, dev)
+    del ins, gy, leaves
+    torch.cuda.empty_cache()
+    t1 = 0.0
+    if rank == 0:
+        ins, gy = make_ss_inputs(cfg, dev, seed=3100, L=Lt)
+        leaves = [t.clone().requires_grad_(True) for t in ins]
+
+        def one_gpu():
+            for t in leaves:
+                t.grad = None
+            u, delta, A, Bm, Cm, Dv = leaves
+            h, outs = None, []
+            for c in range(TRAIN_CHUNKS):
+                sl = slice(c * Lc, (c + 1) * Lc)
+                o, h = SelectiveScanCudaFunction.apply(u[:, sl], delta[:, sl], A, Bm[:, sl], Cm[:, sl], Dv, h)
+                outs.append(o)
+            torch.cat(outs, dim=1).backward(gy)
+
+        t1 = time_fn(one_gpu)
+        del ins, gy, leaves
+        torch.cuda.empty_cache()
+    barrier_sync(world, dev)
+    t1 = max_over_ranks(t1, world, dev)
+    es = torch.tensor([], dtype=cfg["dtype"]).element_size()
+    return {"workload": f"config 4's first {TRAIN_CHUNKS} chunks ({Lt} tokens, fp32, B=1, D=2048) trained: "
+                        "forward + backward of sharding.sequence_sharded_scan, split along L",
+            "ranks": world, "scaling": "strong", "ms_per_step": ms,
+            "value": ss_bytes(B, Lt, D, es, "fwdbwd") / (ms / 1e3) / 1e9, "unit": "GB/s",
+            "one_gpu_chained_ms": t1, "speedup_vs_one_gpu_chained": t1 / ms if ms > 0 else None,
+            "note": "collectives per step: one all-gather (forward), one all-gather and one "
+                    "all-reduce (backward); one GPU: the chunks chained through h_prev / h_last"}
 
 
 _JSON_FD = None
