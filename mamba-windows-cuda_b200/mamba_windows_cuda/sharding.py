@@ -106,6 +106,17 @@ def _cuda_fixup(delta, A, C_ssm, h_in, decay, out, h_last, end=None, dpre=None):
         _ops.ss_fixup(delta, A, C_ssm, h_in, decay, out, h_last, dprefix=dpre)
 
 
+def _prep_cuda(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev):
+    """The reference's input checks (mamba_cuda.py:186-238: CUDA tensors, one dtype, the
+    shapes) and contiguous copies where needed, as the single-GPU ops do: the CUDA entry points
+    take raw pointers of contiguous tensors (a time slice of a (B, L, D) tensor with B > 1 is
+    not contiguous)."""
+    from . import _ops
+    _ops.check_ss_inputs(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev)
+    return [t.contiguous() for t in (u, delta, A, B_ssm, C_ssm, D_ssm)] + [
+        h_prev.contiguous() if h_prev is not None else None]
+
+
 def _split_local(res):
     """(out, h_last, decay, end32, dprefix) from a local scan's result; stand-ins that return
     three values give their h_last as the end state and no prefix records."""
@@ -157,6 +168,9 @@ def sequence_sharded_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=None, *, g
     import torch.distributed as dist
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
+    if local_scan is None and fixup is None:
+        u, delta, A, B_ssm, C_ssm, D_ssm, h_prev = _prep_cuda(u, delta, A, B_ssm, C_ssm, D_ssm,
+                                                               h_prev if rank == 0 else None)
     local_scan = local_scan or _cuda_local_scan
     fixup = fixup or _cuda_fixup
 
@@ -187,6 +201,8 @@ def emulated_sequence_sharded_forward(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=N
     (same local scans, carry fold and fixup as the multi-process path; for tests and for
     checking the fixup without several GPUs). Takes the whole sequence; returns
     ``(out, h_last)`` of the whole sequence."""
+    if local_scan is None and fixup is None:
+        u, delta, A, B_ssm, C_ssm, D_ssm, h_prev = _prep_cuda(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev)
     local_scan = local_scan or _cuda_local_scan
     fixup = fixup or _cuda_fixup
     L = u.shape[1]
@@ -373,6 +389,10 @@ def sequence_sharded_scan(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev=None, *, grou
     (like the single-GPU training forward). ``local_forward``, ``fixup``, ``local_backward``
     and ``local_adjoint`` default to the CUDA entry points; the CPU tests pass float64
     stand-ins."""
+    if local_forward is None and fixup is None and local_backward is None and local_adjoint is None:
+        import torch.distributed as dist
+        u, delta, A, B_ssm, C_ssm, D_ssm, h_prev = _prep_cuda(
+            u, delta, A, B_ssm, C_ssm, D_ssm, h_prev if dist.get_rank(group) == 0 else None)
     hooks = (local_forward or _cuda_train_forward_local, fixup or _cuda_train_fixup,
              local_backward or _cuda_train_backward_local, local_adjoint or _cuda_train_adjoint_local)
     return _SequenceShardedScanFn.apply(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev, group, hooks)
@@ -387,6 +407,9 @@ def emulated_sequence_sharded_training(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev,
     process on one device (the same phases as ``sequence_sharded_scan``; for tests). Takes the
     whole sequence, ``dout`` for the whole output and ``dh_last`` for the sequence's h_last.
     Returns ``(out, h_last, grads)`` with grads a dict of du, ddelta, dA, dB, dC, dD, dh_prev."""
+    if local_forward is None and fixup is None and local_backward is None and local_adjoint is None:
+        u, delta, A, B_ssm, C_ssm, D_ssm, h_prev = _prep_cuda(u, delta, A, B_ssm, C_ssm, D_ssm, h_prev)
+        dout = dout.contiguous()
     lf = local_forward or _cuda_train_forward_local
     fx = fixup or _cuda_train_fixup
     lb = local_backward or _cuda_train_backward_local

@@ -182,3 +182,14 @@ def test_gloo_two_ranks_training_matches_full_backward():
         assert_fp32(got["A"][r], ref["dA"], what=f"dA on rank {r}")
         assert_fp32(got["Dv"][r], ref["dD"], what=f"dD on rank {r}")
     assert_fp32(got["hp"][0], ref["dh_prev"], what="dh_prev (rank 0)")
+
+
+def test_cuda_paths_reject_cpu_tensors():
+    """With the default (CUDA) hooks the sharded entry points apply the reference's input
+    checks (mamba_cuda.py:186-238) before anything reaches the C entry points."""
+    x, dout, dh_last = _train_case(L=16)
+    args = [x[k] for k in ("u", "delta", "A", "Bm", "Cm", "Dv")]
+    with pytest.raises(RuntimeError, match="must be a CUDA tensor"):
+        S.emulated_sequence_sharded_forward(*args, x["h_prev"], world=2)
+    with pytest.raises(RuntimeError, match="must be a CUDA tensor"):
+        S.emulated_sequence_sharded_training(*args, x["h_prev"], dout, dh_last, world=2)
