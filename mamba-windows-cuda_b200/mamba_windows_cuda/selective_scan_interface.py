@@ -31,10 +31,12 @@ class SelectiveScanFnEx(torch.autograd.Function):
         if D is None:
             D = torch.zeros(u.shape[2], dtype=u.dtype, device=u.device)
         _ops.check_ss_inputs(u, delta, A, B, C, D, h_prev)
-        if z is not None and (z.shape != u.shape or z.dtype != u.dtype):
-            raise RuntimeError("z must match u in shape and dtype")
-        if delta_bias is not None and (delta_bias.shape != (u.shape[2],) or delta_bias.dtype != u.dtype):
-            raise RuntimeError("delta_bias must be (D,) with u's dtype")
+        if z is not None and (not isinstance(z, torch.Tensor) or z.shape != u.shape or z.dtype != u.dtype
+                              or z.device != u.device):
+            raise RuntimeError("z must match u in shape, dtype and device")
+        if delta_bias is not None and (not isinstance(delta_bias, torch.Tensor) or delta_bias.shape != (u.shape[2],)
+                                       or delta_bias.dtype != u.dtype or delta_bias.device != u.device):
+            raise RuntimeError("delta_bias must be (D,) with u's dtype and device")
         u, delta, A, B, C, D = [t.contiguous() for t in (u, delta, A, B, C, D)]
         z = z.contiguous() if z is not None else None
         delta_bias = delta_bias.contiguous() if delta_bias is not None else None

@@ -108,3 +108,15 @@ def test_extended_scan_without_transforms_equals_plain_scan():
     a = selective_scan_fn(*args)
     b = mwc.SelectiveScanCuda()(*args)
     assert torch.equal(a, b)
+
+
+def test_extended_scan_rejects_z_and_bias_off_device():
+    """z and delta_bias on the host (with u on the GPU) are rejected before any launch."""
+    _need_gpu()
+    from mamba_windows_cuda.selective_scan_interface import selective_scan_fn
+    x = make_inputs(1, 32, 16, torch.float32, seed=53, device="cuda")
+    args = [x[k] for k in ("u", "delta", "A", "Bm", "Cm", "Dv")]
+    with pytest.raises(RuntimeError, match="z must match u"):
+        selective_scan_fn(*args, z=torch.zeros(1, 32, 16))
+    with pytest.raises(RuntimeError, match="delta_bias must be"):
+        selective_scan_fn(*args, delta_bias=torch.zeros(16))
