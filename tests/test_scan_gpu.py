@@ -443,3 +443,35 @@ def test_persistent_forward_is_deterministic_and_ckpt_only(mwc):
     _, h3, c3, _ = _ops.ss_forward(*args, want_out=False, want_h_last=True, want_ckpt=True)
     assert torch.equal(o1, o2) and torch.equal(h1, h2) and torch.equal(c1, c2)
     assert torch.equal(h1, h3) and torch.equal(c1, c3)
+
+
+@pytest.mark.parametrize("B,L,D,case", [(4, 512, 5120, "posA"), (1, 4096, 512, "posA"),
+                                        (4, 512, 5120, "negdelta"), (1, 4096, 512, "negdelta")])
+def test_persistent_paths_with_positive_exponents(mwc, B, L, D, case):
+    """The clamped copies of the persistent step loops (chosen per tile when some A > 0 or
+    some delta < 0 makes an exponent positive): chained segments (160 chains) and the
+    few-chain split passes, float32 fwd + bwd against the oracle with the clamp."""
+    from mamba_windows_cuda import _ops
+    path = _ops.plan(B, L, D, torch.float32)["path"]
+    assert path == ("chained" if B * D // 128 >= 148 else "split")
+    g = torch.Generator().manual_seed(61)
+    x = make_inputs(B, L, D, torch.float32, seed=61, dist="c1", with_state=True)
+    if case == "posA":   # small positive A on some states: slow growth, no overflow over L
+        x["A"] = -torch.rand(D, 16, generator=g) + 0.02
+        x["delta"] = torch.nn.functional.softplus(torch.randn(B, L, D, generator=g) * 0.5 - 2.0)
+    else:                # delta of both signs with A < 0
+        x["delta"] = torch.randn(B, L, D, generator=g) * 0.02
+    x = {k: v.cuda() for k, v in x.items()}
+    leaves = [x[k].clone().requires_grad_(True) for k in ("u", "delta", "A", "Bm", "Cm", "Dv")]
+    hp = x["h_prev"].clone().requires_grad_(True)
+    out, h_last = mwc.SelectiveScanCuda().forward_with_state(*leaves, hp)
+    (out * x["g"]).sum().backward()
+    torch.cuda.synchronize()
+    n = [np64(t) for t in leaves]
+    o64, h64 = O.ss_fwd(*n, np64(hp), clamp=True)
+    g64 = O.ss_bwd(*n, np64(x["g"]), np64(hp), None, clamp=True)
+    assert_fp32(out, o64, what="out")
+    assert_fp32(h_last, h64, what="h_last")
+    for name, t in zip(("du", "ddelta", "dA", "dB", "dC", "dD"), leaves):
+        assert_fp32(t.grad, g64[name], what=name)
+    assert_fp32(hp.grad, g64["dh_prev"], what="dh_prev")
