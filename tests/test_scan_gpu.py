@@ -475,3 +475,30 @@ def test_persistent_paths_with_positive_exponents(mwc, B, L, D, case):
     for name, t in zip(("du", "ddelta", "dA", "dB", "dC", "dD"), leaves):
         assert_fp32(t.grad, g64[name], what=name)
     assert_fp32(hp.grad, g64["dh_prev"], what="dh_prev")
+
+
+@pytest.mark.parametrize("B,L,D", [(4, 512, 5064), (1, 2048, 1000)])
+def test_persistent_fp16_partial_channel_block(mwc, B, L, D):
+    """D not a multiple of 128 (the last 128-channel block partial) on the persistent
+    kernels in float16: chained segments (160 chains) and the few-chain split passes, fwd +
+    bwd against the oracle (per-element results elementwise atol 2e-2 / rtol 1e-2, the sums
+    dA / dB / dC / dD with atol scaled by their magnitude)."""
+    from mamba_windows_cuda import _ops
+    assert _ops.plan(B, L, D, torch.float16)["path"] != "generic"
+    x = make_inputs(B, L, D, torch.float16, seed=67, dist="c3", with_state=True, device="cuda")
+    leaves = [x[k].clone().requires_grad_(True) for k in ("u", "delta", "A", "Bm", "Cm", "Dv")]
+    hp = x["h_prev"].clone().requires_grad_(True)
+    out, h_last = mwc.SelectiveScanCuda().forward_with_state(*leaves, hp)
+    (out * x["g"]).sum().backward()
+    torch.cuda.synchronize()
+    n = [np64(t) for t in leaves]
+    o64, h64 = O.ss_fwd(*n, np64(hp))
+    g64 = O.ss_bwd(*n, np64(x["g"]), np64(hp), None)
+    assert_fp16(out, o64, what="out")
+    assert_fp16(h_last, h64, what="h_last")
+    for name, t in zip(("du", "ddelta"), leaves[:2]):
+        assert_fp16(t.grad, g64[name], what=name)
+    for name, t in zip(("dA", "dB", "dC", "dD"), leaves[2:]):
+        ref = g64[name]
+        assert_fp16(t.grad, ref, what=name, atol=2e-2 * max(1.0, float(np.abs(ref).max())))
+    assert_fp16(hp.grad, g64["dh_prev"], what="dh_prev")
