@@ -316,10 +316,11 @@ def _train_bwd_phase1(rank, world, ins, h_start, ckpt, dout, dh_last, local_back
 
 def _train_bwd_phase2(rank, world, gathered, ins, h_start, ckpt, grads, dout, dh_last, local_backward):
     """After the all-gather of (decay, q0) records: this rank's gradients. The last rank's
-    local reverse scan is already complete. Every other rank scans its range again with the
-    whole adjoint entering at the end, dh_last + Q (float32), rather than adding a separate
-    scan of Q's share: the two shares can be large with opposite signs next to the range end,
-    and rounding each to a 16-bit type before the sum would lose the difference."""
+    local reverse scan is already complete. Every other rank runs its reverse scan now, with
+    the whole adjoint entering at the range end, dh_last + Q (float32), in one scan rather
+    than as a scan of its own terms plus a scan of Q's share: the two shares can be large
+    with opposite signs next to the range end, and rounding each to a 16-bit type before the
+    sum would lose the difference."""
     if rank >= world - 1:
         return list(grads)
     later = torch.flip(gathered[rank + 1:], dims=[0])   # ranks world-1 .. rank+1
