@@ -91,7 +91,10 @@ MWC_API int64_t mwc_ss_bwd_workspace_bytes(int64_t B, int64_t L, int64_t D, int 
  * for (B, L, D, dtype) on the current device, assuming 16-byte-aligned buffers. Writes
  * info[0] = path (MWC_PATH_*), info[1] = K (time segments per 128-channel chain),
  * info[2] = segment length in time tiles (32 steps forward, 16 backward; the segmented
- * generic path: steps), info[3] = CTAs of the main launch. For tests and tuning; no
+ * generic path: steps), info[3] = CTAs of the main launch. The chained forward
+ * (MWC_PATH_CHAINED, backward = 0) instead gives each CTA one run of the chains'
+ * concatenated tiles: info[2] is the longest run, and info[1] is 2 when a run boundary
+ * cuts a chain (its head and tail run on two CTAs), else 1. For tests and tuning; no
  * counterpart in the reference (its kernels had one fixed launch shape).
  */
 enum mwc_path { MWC_PATH_GENERIC = 0, MWC_PATH_CHAINED = 1, MWC_PATH_SPLIT = 2 };

@@ -120,15 +120,17 @@ struct PFwdArgs {
     // of the prefix sum through each step; the sequence-sharding fixup uses it to skip the
     // part of a range where the incoming state has decayed away
     float* dpre;
-    float* hand;     // (chains, K, 128, 17): state + sum(delta) handed to the next segment
-    int* flags;      // (chains, K) segment-done flags
-    int* counter;    // unit queue head
+    float* hand;     // (chains, K, 128, 17): state + sum(delta) handed to the next unit
+                     // (mode 0: record c of chain c, written by the head of a cut chain)
+    int* flags;      // (chains, K) unit-done flags (mode 0: flag c)
+    int* counter;    // unit queue head (mode 0: run index, in the order the CTAs start)
     int* err;        // bounded-wait error word
     int B, L, D;
     int nblk, nchains, K, seg_tiles, ntiles, nck;
     int has_out;
     int G, cpg;      // B / C groups (B_ssm, C_ssm are (B, L, G, 16)) and channels per group
-    // 0: chained segments (segment k waits for the record segment k-1 publishes);
+    // 0: chained: one run of the chains' concatenated tiles per CTA; the tail of a chain cut
+    //    between two runs waits for the record the head publishes;
     // 1: state only: segments 0..K-2 scan independently (segment 0 from h_prev, the others
     //    from zero) and each writes its end state and delta sum as its record;
     // 2: seeded: the records already hold each segment's incoming state and delta prefix sum
@@ -137,7 +139,7 @@ struct PFwdArgs {
 };
 
 struct PersistPlan {
-    bool ok;        // enough chains (>= SMs) for the queue to keep every SM busy
+    bool ok;        // chained: enough chains (>= SMs) for one run per SM; split: segments fit
     int nblk, nchains, ntiles, K, seg_tiles, grid;
 };
 

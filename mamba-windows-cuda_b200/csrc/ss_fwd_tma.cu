@@ -1,20 +1,23 @@
 // Persistent, warp-specialized, TMA-pipelined forward selective scan for sm_100a.
 //
-// Work decomposition: a "chain" is one batch row x 128 channels over all of L; each chain
-// is cut into K time segments. Units (segment k of chain c) are taken from a global
-// atomic counter in segment-major order by one persistent CTA per SM, so the B*D/128
-// chains spread evenly over the SMs even when there are only slightly more chains than SMs
-// (config 3: 160 chains on 148 SMs). Segment k starts from the state segment k-1
-// published (8 per-warp release increments of a flag); because segments are taken in
-// order, the publisher is always a CTA that is already running, so every wait ends (and
-// each wait is bounded).
+// Work decomposition: a "chain" is one batch row x 128 channels over all of L, cut into
+// 32-step tiles. With at least as many chains as SMs (the chained path, mode 0), one
+// persistent CTA per SM takes an equal run of the chains' concatenated tiles (config 3:
+// 160 chains x 64 tiles on 148 SMs, 69-70 tiles per CTA). A chain cut between two runs is
+// handed over once: the earlier run scans that chain's head first and publishes its end
+// state (8 per-warp release increments of a flag); the later run scans the chain's tail
+// last, so the record is ready or nearly ready when it is needed (each wait is bounded).
+// A dynamic queue of K time segments per chain instead leaves no slack when the chains
+// barely outnumber the SMs: most units start one wave after the unit they depend on.
+// With fewer chains than SMs the split passes (modes 1 / 2) take K independent segments
+// per chain from an atomic queue.
 //
 // CTA = 10 warps, no CTA-wide barrier after set-up; mbarriers connect the roles:
 //   * warps 0-7 (compute): thread = (channel, half): 8 of the channel's 16 states in
 //     registers as 4 float2 pairs (packed FFMA2), the two halves' <C, h> meet through one
 //     shuffle; ex2 with log2(e) folded into A; y to a staging tile, float32 checkpoints
 //     every 16 steps straight to global memory;
-//   * warp 8 (producer): unit queue, hand-off waits, TMA loads of u / delta (32 x 128),
+//   * warp 8 (producer): the CTA's units, hand-off waits, TMA loads of u / delta (32 x 128),
 //     B / C (32 x 16) and the segment's incoming state (1-D bulk copy) into a ring of
 //     stages (full / empty mbarriers);
 //   * warp 9 (helper): float32 copies of B / C for fp16 inputs, and the TMA stores of y
@@ -42,10 +45,6 @@ constexpr int PF_NCW = PF_CPB * PF_LPC / 32; // compute warps
 constexpr int PF_NT = (PF_NCW + 2) * 32;     // + producer warp + helper warp
 constexpr int PF_HAND = PF_CPB * (NSTATE + 1);  // floats of one segment hand-off record
 static_assert(PF_LT % CK == 0, "a forward tile holds whole checkpoint chunks");
-#ifndef MWC_FWD_MIN_SEG_TILES
-#define MWC_FWD_MIN_SEG_TILES 8   // shortest chained segment (in 32-step tiles) the planner may
-                                  // pick: fewer hand-offs (config 3: 8 segments, 1.5% faster than 11)
-#endif
 #ifndef MWC_FWD_SPLIT_MIN_SEG_TILES
 #define MWC_FWD_SPLIT_MIN_SEG_TILES 2   // shortest independent segment of the few-chain split
 #endif
@@ -70,10 +69,19 @@ struct __align__(128) PFwdSmem {
     float Bf[sizeof(T) == 2 ? ST : 1][PF_LT][NSTATE];            // float32 B / C (fp16 only)
     float Cf[sizeof(T) == 2 ? ST : 1][PF_LT][NSTATE];
     uint64_t full[ST], conv[ST], empty[ST], yfull[2], yempty[2];
+    // the stage's unit: chain (-1: no more units), tile within the unit, the unit's first
+    // tile in the chain and its tile count, where its incoming state comes from (RIN_*, or a
+    // record index) and where its end state goes (ROUT_*, or a record index)
     int unit[ST];
     int tile[ST];
+    int first[ST], ntl[ST], rin[ST], rout[ST];
     int dpos[ST];   // helper: 1 when no delta of the stage's tile has its sign bit set
 };
+
+constexpr int RIN_START = -2;   // the chain's start: h_prev (or zero)
+constexpr int RIN_ZERO = -1;    // zero (state-only segments after the first)
+constexpr int ROUT_END = -1;    // the chain's end: h_last / decay
+constexpr int ROUT_NONE = -2;   // nothing (seeded segments before the last)
 
 // One block of 8 steps for the lane's 8 states (4 float2 pairs). CLAMP applies the
 // safe_exp upper clamp per state; the caller takes the unclamped variant only when every
@@ -143,8 +151,6 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
         return;
     }
     const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
-    const int total = p.nchains * (p.mode == 1 ? p.K - 1 : p.K);   // state-only: no last segment
-    auto unit_tiles = [&](int k) { return min(p.seg_tiles, p.ntiles - k * p.seg_tiles); };
 
     if (tid == 0) {
         for (int i = 0; i < ST; ++i) {
@@ -169,34 +175,88 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
         prefetch_tmap(&p.tm_C);
         const unsigned tile_bytes =
             (unsigned)((2 * PF_LT * PF_CPB + (p.has_out ? 2 : 1) * PF_LT * NSTATE) * sizeof(T));
-        int pu = -1, ptile = 0, ptiles = 0;
+        // the unit being issued: chain pc, tiles pfirst .. pfirst + pntl - 1 of it, the source
+        // of its incoming state (prin) and the destination of its end state (prout)
+        int pc = -1, ptile = 0, pfirst = 0, pntl = 0, prin = RIN_START, prout = ROUT_END;
+        // Chained (mode 0): static runs. The chains' tiles, concatenated, are cut into one
+        // equal run per CTA, [rs, re); a run is at least one chain long, so a chain is cut at
+        // most once, into a head (ending a run) and a tail (starting the next). A run issues
+        // the head it ends with first (its record is what the next run's tail waits for), then
+        // its whole chains, then the tail it starts with: every tail then waits for a head
+        // that the previous run finished first. Run indices come from the counter in the
+        // order the CTAs start, so the run a tail waits for belongs to a CTA already running.
+        int64_t rs = 0, re = 0;
+        int nxt = 0;   // units of the run issued so far
+        if (p.mode == 0) {
+            const int64_t all = (int64_t)p.nchains * p.ntiles;
+            const int64_t r = atomicAdd(p.counter, 1);
+            rs = all * r / gridDim.x;
+            re = all * (r + 1) / gridDim.x;
+        }
+        const int total = p.nchains * (p.mode == 1 ? p.K - 1 : p.K);   // state-only: no last segment
+        auto next_unit = [&]() -> bool {
+            if (p.mode == 0) {
+                if (rs >= re) return false;
+                const int c_lo = (int)(rs / p.ntiles), c_hi = (int)((re - 1) / p.ntiles);
+                const int tail = (int)(rs % p.ntiles), head = (int)(re % p.ntiles);
+                const int f_lo = c_lo + (tail != 0 ? 1 : 0), f_hi = c_hi - (head != 0 ? 1 : 0);
+                int j = nxt++;
+                if (head != 0) {
+                    if (j == 0) {
+                        pc = c_hi; pfirst = 0; pntl = head; prin = RIN_START; prout = c_hi;
+                        return true;
+                    }
+                    --j;
+                }
+                if (j <= f_hi - f_lo) {
+                    pc = f_lo + j; pfirst = 0; pntl = p.ntiles; prin = RIN_START; prout = ROUT_END;
+                    return true;
+                }
+                if (tail != 0 && j == f_hi - f_lo + 1) {
+                    pc = c_lo; pfirst = tail; pntl = p.ntiles - tail; prin = c_lo; prout = ROUT_END;
+                    return true;
+                }
+                return false;
+            }
+            // split passes (modes 1 / 2): K independent segments per chain from the queue
+            const int pu = atomicAdd(p.counter, 1);
+            if (pu >= total) return false;
+            const int k = pu / p.nchains;
+            pc = pu % p.nchains;
+            pfirst = k * p.seg_tiles;
+            pntl = min(p.seg_tiles, p.ntiles - pfirst);
+            prin = k == 0 ? RIN_START : p.mode == 1 ? RIN_ZERO : pc * p.K + k - 1;
+            prout = k == p.K - 1 ? ROUT_END : p.mode == 1 ? pc * p.K + k : ROUT_NONE;
+            return true;
+        };
         for (int it = 0;; ++it) {
             const int st = it % ST;
             mbar_wait(&s.empty[st], ((unsigned)(it / ST) & 1u) ^ 1u, p.err);
-            if (pu < 0 || ptile == ptiles) {
-                pu = atomicAdd(p.counter, 1);
-                if (pu >= total) {
+            if (pc < 0 || ptile == pntl) {
+                if (!next_unit()) {
                     s.unit[st] = -1;
                     mbar_arrive(&s.full[st]);
                     return;
                 }
                 ptile = 0;
-                ptiles = unit_tiles(pu / p.nchains);
             }
-            const int c = pu % p.nchains, k = pu / p.nchains;
-            const int b = c / p.nblk, blk = c % p.nblk;
-            const int t0 = (k * p.seg_tiles + ptile) * PF_LT;
-            s.unit[st] = pu;
+            const int b = pc / p.nblk, blk = pc % p.nblk;
+            const int t0 = (pfirst + ptile) * PF_LT;
+            s.unit[st] = pc;
             s.tile[st] = ptile;
+            s.first[st] = pfirst;
+            s.ntl[st] = pntl;
+            s.rin[st] = prin;
+            s.rout[st] = prout;
             unsigned bytes = tile_bytes;
-            const bool need_hand = ptile == 0 && k > 0 && p.mode != 1;
-            const bool need_hprev = ptile == 0 && k == 0 && p.h_prev != nullptr;
+            const bool need_hand = ptile == 0 && prin >= 0;
+            const bool need_hprev = ptile == 0 && prin == RIN_START && p.h_prev != nullptr;
             const int nch = min(PF_CPB, p.D - blk * PF_CPB);
             const unsigned rows_bytes = (unsigned)(nch * NSTATE * sizeof(T));
             if (ptile == 0) bytes += rows_bytes + (unsigned)(nch * sizeof(T));
             if (need_hprev) bytes += rows_bytes;
             if (need_hand) {
-                if (p.mode == 0) flag_wait(&p.flags[c * p.K + k - 1], PF_NCW, p.err);
+                if (p.mode == 0) flag_wait(&p.flags[prin], PF_NCW, p.err);
                 // the record was written with generic-proxy stores (made visible by the
                 // acquire above); the bulk copy below reads it through the async proxy
                 fence_proxy_async_global();
@@ -220,8 +280,7 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
             tma_load_3d(&s.Bt[st][0][0], &p.tm_B, &s.full[st], gx, t0, b);
             if (p.has_out) tma_load_3d(&s.Ct[st][0][0], &p.tm_C, &s.full[st], gx, t0, b);
             if (need_hand)
-                bulk_load_1d(&s.hin[st][0], p.hand + (int64_t)(c * p.K + k - 1) * PF_HAND,
-                             PF_HAND * 4, &s.full[st]);
+                bulk_load_1d(&s.hin[st][0], p.hand + (int64_t)prin * PF_HAND, PF_HAND * 4, &s.full[st]);
             ++ptile;
         }
     }
@@ -236,10 +295,9 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
             const int unit = s.unit[st];
             int b = 0, blk = 0, t0 = 0;
             if (unit >= 0) {
-                const int c = unit % p.nchains, k = unit / p.nchains;
-                b = c / p.nblk;
-                blk = c % p.nblk;
-                t0 = (k * p.seg_tiles + s.tile[st]) * PF_LT;
+                b = unit / p.nblk;
+                blk = unit % p.nblk;
+                t0 = (s.first[st] + s.tile[st]) * PF_LT;
                 if constexpr (HALF) {
                     for (int idx = lane; idx < PF_LT * NSTATE; idx += 32) {
                         (&s.Bf[st][0][0])[idx] = to_f((&s.Bt[st][0][0])[idx]);
@@ -303,10 +361,10 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
         const int unit = s.unit[st];
         if (unit < 0) break;
         const int tile = s.tile[st];
-        const int c = unit % p.nchains, k = unit / p.nchains;
-        const int b = c / p.nblk, blk = c % p.nblk;
-        const int t0 = (k * p.seg_tiles + tile) * PF_LT;
-        const bool last = tile == unit_tiles(k) - 1;
+        const int b = unit / p.nblk, blk = unit % p.nblk;
+        const int t0 = (s.first[st] + tile) * PF_LT;
+        const int rin = s.rin[st], rout = s.rout[st];
+        const bool last = tile == s.ntl[st] - 1;
 
         if (tile == 0) {  // unit start: parameters and incoming state (staged by the producer)
             d = (int64_t)blk * PF_CPB + ch;
@@ -320,11 +378,11 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
             }
             a_nonpos = __all_sync(FULL, nonpos);
             Dd = dv ? to_f(s.Dt[st][ch]) : 0.f;
-            if (k == 0 || p.mode == 1) {   // state-only segments after the first start from zero
+            if (rin < 0) {   // the chain's start, or a state-only segment (from zero)
                 sumd = 0.f;
 #pragma unroll
                 for (int j = 0; j < PF_NP; ++j) h2[j] = make_float2(0.f, 0.f);
-                if (k == 0 && p.h_prev != nullptr && dv) {
+                if (rin == RIN_START && p.h_prev != nullptr && dv) {
 #pragma unroll
                     for (int j = 0; j < PF_NP; ++j)
                         h2[j] = make_float2(to_f(s.Ht[st][ch][n0 + 2 * j]), to_f(s.Ht[st][ch][n0 + 2 * j + 1]));
@@ -418,22 +476,20 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
         }
 
         if (last) {
-            if (k < p.K - 1) {
-                if (p.mode != 2) {   // seeded segments find their records already written
-                    float* hs = p.hand + (int64_t)(c * p.K + k) * PF_HAND + ch * (NSTATE + 1);
+            if (rout >= 0) {   // a record for the unit that continues the chain
+                float* hs = p.hand + (int64_t)rout * PF_HAND + ch * (NSTATE + 1);
 #pragma unroll
-                    for (int j = 0; j < PF_NP; ++j) {
-                        hs[n0 + 2 * j] = h2[j].x;
-                        hs[n0 + 2 * j + 1] = h2[j].y;
-                    }
-                    if (half == 0) hs[NSTATE] = sumd;
-                    if (p.mode == 0) {
-                        __threadfence();
-                        __syncwarp();
-                        if (lane == 0) atomicAdd(&p.flags[c * p.K + k], 1);
-                    }
+                for (int j = 0; j < PF_NP; ++j) {
+                    hs[n0 + 2 * j] = h2[j].x;
+                    hs[n0 + 2 * j + 1] = h2[j].y;
                 }
-            } else if (dv) {
+                if (half == 0) hs[NSTATE] = sumd;
+                if (p.mode == 0) {
+                    __threadfence();
+                    __syncwarp();
+                    if (lane == 0) atomicAdd(&p.flags[rout], 1);
+                }
+            } else if (rout == ROUT_END && dv) {
                 if (p.h_last != nullptr) {
                     T* hl = static_cast<T*>(p.h_last) + ((int64_t)b * p.D + d) * NSTATE + n0;
 #pragma unroll
@@ -523,26 +579,19 @@ PersistPlan plan_persistent(int64_t B, int64_t L, int64_t D, int num_sms) {
     pl.nblk = (int)((D + PF_CPB - 1) / PF_CPB);
     pl.nchains = (int)(B * pl.nblk);
     pl.ntiles = (int)((L + PF_LT - 1) / PF_LT);
-    pl.ok = pl.nchains >= num_sms;
-    int best_k = 1;
-    double best = -1.0;
-    for (int K = 1; K <= pl.ntiles; ++K) {
-        const int seg = (pl.ntiles + K - 1) / K;
-        const int keff = (pl.ntiles + seg - 1) / seg;
-        if (keff != K) continue;
-        if (K > 1 && seg < MWC_FWD_MIN_SEG_TILES) break;
-        const int64_t U = (int64_t)pl.nchains * K;
-        const int64_t G = std::min<int64_t>(num_sms, U);
-        const int64_t waves = (U + G - 1) / G;
-        const double eff = (double)U / (double)(G * waves);
-        if (eff > best + 0.01) {
-            best = eff;
-            best_k = K;
+    pl.ok = num_sms > 0 && pl.nchains >= num_sms;
+    if (!pl.ok) return pl;
+    // one run of the concatenated tiles per SM (seg_tiles: the longest run); K = 2 when a
+    // run boundary cuts a chain (a chain is cut at most once: runs are >= one chain long)
+    pl.grid = num_sms;
+    const int64_t T = (int64_t)pl.nchains * pl.ntiles;
+    pl.seg_tiles = (int)((T + pl.grid - 1) / pl.grid);
+    pl.K = 1;
+    for (int r = 1; r < pl.grid; ++r)
+        if ((T * r / pl.grid) % pl.ntiles != 0) {
+            pl.K = 2;
+            break;
         }
-    }
-    pl.K = best_k;
-    pl.seg_tiles = (pl.ntiles + best_k - 1) / best_k;
-    pl.grid = (int)std::min<int64_t>(num_sms, (int64_t)pl.nchains * pl.K);
     return pl;
 }
 

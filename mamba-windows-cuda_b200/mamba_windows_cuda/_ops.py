@@ -147,9 +147,11 @@ PATHS = {0: "generic", 1: "chained", 2: "split"}
 
 def plan(B: int, L: int, D: int, dtype: torch.dtype, backward: bool = False) -> dict:
     """The launch plan the forward (or backward) picks for (B, L, D) on the current device,
-    for 16-byte-aligned buffers (mwc_ss_plan): path ("chained": persistent kernel with K
-    chained time segments per 128-channel chain; "split": independent segments + fold;
-    "generic": the non-TMA kernels), K, segment length (tiles), CTAs."""
+    for 16-byte-aligned buffers (mwc_ss_plan): path ("chained": persistent kernel over
+    chained 128-channel chains; "split": independent segments + fold; "generic": the
+    non-TMA kernels), K, seg, CTAs. Chained forward: one run of the chains' concatenated
+    32-step tiles per CTA, seg = the longest run, K = 2 when a run boundary cuts a chain
+    (else 1). Chained backward and split paths: K time segments of seg tiles per chain."""
     lib = _lib.load()
     info = (ctypes.c_int32 * 4)()
     _lib.check(lib.mwc_ss_plan(B, L, D, _DTYPES[dtype], int(bool(backward)), info), "plan query")

@@ -64,14 +64,21 @@ def test_size_queries(lib):
 
 def test_plan_query(lib):
     """mwc_ss_plan reports the path the entry points take (148 SMs assumed without a GPU):
-    the benchmark's config 3 and config 2 run chained persistent segments (K > 1), config 4's
-    chunk the few-chain split passes, short few-channel shapes the generic kernels."""
+    the benchmark's config 3 and config 2 run the chained persistent kernels, config 4's
+    chunk the few-chain split passes, short few-channel shapes the generic kernels. The
+    chained forward gives each SM one run of the chains' concatenated 32-step tiles (seg =
+    the longest run); K = 2 when a run boundary cuts a chain, 1 when every run is whole
+    chains. The chained backward cuts each chain into K segments of seg 16-step tiles."""
     from mamba_windows_cuda import _ops
     f16 = torch.float16
     p3f, p3b = _ops.plan(4, 2048, 5120, f16), _ops.plan(4, 2048, 5120, f16, backward=True)
-    assert p3f["path"] == "chained" and p3f["K"] > 1 and p3f["K"] * p3f["seg"] * 32 >= 2048
+    # config 3: 160 chains x 64 tiles over 148 runs of 69-70 tiles
+    assert p3f == {"path": "chained", "K": 2, "seg": 70, "grid": 148}, p3f
     assert p3b["path"] == "chained" and p3b["K"] > 1 and p3b["K"] * p3b["seg"] * 16 >= 2048
-    assert _ops.plan(8, 2048, 4096, f16)["K"] > 1
+    assert _ops.plan(8, 2048, 4096, f16)["K"] == 2
+    # one chain per SM: whole chains, nothing handed over
+    assert _ops.plan(4, 2048, 4736, f16) == {"path": "chained", "K": 1, "seg": 64, "grid": 148}
+    assert _ops.plan(2, 4096, 18944, f16) == {"path": "chained", "K": 1, "seg": 256, "grid": 148}
     assert _ops.plan(1, 65536, 2048, torch.float32)["path"] == "split"
     assert _ops.plan(2, 256, 5120, f16)["path"] == "generic"
     # rows of D x 2 bytes that are not a multiple of 16 bytes never take the TMA paths

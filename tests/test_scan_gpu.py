@@ -370,6 +370,33 @@ def test_persistent_forward_many_chains(mwc, dtype, D, L):
             assert_fp16(grads[k2], ref[k2], k2, atol=2e-2 * scale, rtol=1e-2)
 
 
+@pytest.mark.parametrize("extra,B", [(0, 2), (1, 1), (37, 1)])
+def test_persistent_forward_static_runs_edges(mwc, extra, B):
+    """The chained forward gives each SM one equal run of the chains' concatenated tiles. With
+    exactly one chain per SM no chain is cut (K = 1); with one chain more than the SMs some
+    runs are exactly one chain long, so a tail waits for a head finished at the same time;
+    with 37 more, runs end and start inside chains throughout. Forward and gradients
+    against the float64 oracle, fp32."""
+    from mamba_windows_cuda import _ops
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    chains = sms + extra
+    if chains % B:
+        pytest.skip("chain count not divisible by the batch")
+    D, L = chains // B * 128, 512
+    plan = _ops.plan(B, L, D, torch.float32)
+    assert plan["path"] == "chained" and plan["K"] == (1 if extra == 0 else 2), plan
+    x = make_inputs(B, L, D, torch.float32, seed=41 + extra, with_state=True, device="cuda")
+    args = [x[k] for k in ("u", "delta", "A", "Bm", "Cm", "Dv")]
+    out, h_last, _, _ = _ops.ss_forward(*args, x["h_prev"], want_h_last=True)
+    ref_out, ref_h = oracle_fwd(x, x["h_prev"])
+    assert_fp32(out, ref_out, what="out")
+    assert_fp32(h_last, ref_h, what="h_last")
+    _, _, grads = run_stateful(mwc, x, x["h_prev"], x["gh"])
+    ref = oracle_bwd(x, x["h_prev"], x["gh"])
+    for k2 in GRADS + ("dh_prev",):
+        assert_fp32(grads[k2], ref[k2], what=k2)
+
+
 @pytest.mark.parametrize("dtype,B,L,D,dist", [(torch.float32, 1, 4096, 2048, "c4"),
                                                (torch.float16, 2, 3000, 640, "c1"),
                                                (torch.bfloat16, 1, 2048, 1024, "c1")])
