@@ -472,8 +472,12 @@ __global__ void __launch_bounds__(PB_NT, 1) ss_bwd_persistent_kernel(const __gri
         auto recompute = [&](auto clamp_tag) {
             constexpr bool CLAMP = decltype(clamp_tag)::value;
             // two 4-step blocks per iteration: the second block's loads and exponentials
-            // overlap the first block's serial updates (168 registers, no spills)
-#pragma unroll 2
+            // overlap the first block's serial updates (fp16: 168 registers, no spills).
+            // 168 is the ceiling (the sub-partitions with 3 of the 10 warps hold 3 x 32 x 168
+            // of their 16,384 registers); bfloat16 spilled 116 bytes with two blocks and runs
+            // 3% faster with one (158 registers, no spills)
+            constexpr int RU = std::is_same<T, __nv_bfloat16>::value ? 1 : 2;
+#pragma unroll RU
         for (int i0 = 0; i0 < PB_LT; i0 += 4) {
             float dt[4][2], uu[4][2];
             float4 B4[4];
