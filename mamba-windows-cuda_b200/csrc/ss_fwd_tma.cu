@@ -433,7 +433,20 @@ __global__ void __launch_bounds__(PF_NT, 1) ss_fwd_persistent_kernel(const __gri
                         }
                     }
                     fwd_block8<CLAMP>(h2, A2v, dtv, uv, Bf + i0 * NSTATE, Cf + i0 * NSTATE, n0, yv);
-                    if constexpr (HAS_OUT) {
+                    if constexpr (HAS_OUT && PF_LPC == 2) {
+                        // the two lanes of a channel finish half the block's steps each (a
+                        // reduce-scatter): lane half 0 steps 0-3, half 1 steps 4-7; the sums
+                        // are the same as one full exchange per step (a + b = b + a)
+                        const bool up = half != 0;
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const float send = up ? yv[j] : yv[j + 4];
+                            const float keep = up ? yv[j + 4] : yv[j];
+                            const float y = keep + __shfl_xor_sync(FULL, send, 1);
+                            const float ur = up ? uv[j + 4] : uv[j];
+                            s.y[yb][i0 + j + 4 * half][ch] = from_f<T>(fmaf(Dd, ur, y));
+                        }
+                    } else if constexpr (HAS_OUT) {
 #pragma unroll
                         for (int r = 0; r < 8; ++r) {
                             float y = yv[r];
